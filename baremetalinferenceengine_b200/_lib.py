@@ -1,0 +1,99 @@
+"""ctypes binding of ``libbm_layer_ops.so`` (the C ABI in ``include/bm_layer_ops.h``).
+
+Loading fails loudly when the library has not been built: there is no CPU or
+PyTorch fallback for any op.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from .build import LIB_PATH
+
+c_int, c_int32, c_int64, c_float, c_double = (ctypes.c_int, ctypes.c_int32, ctypes.c_int64,
+                                              ctypes.c_float, ctypes.c_double)
+c_void_p, c_char_p = ctypes.c_void_p, ctypes.c_char_p
+P_INT32 = ctypes.POINTER(ctypes.c_int32)
+
+BM_OK = 0
+BM_ERR_INVALID_ARGUMENT = 1
+BM_ERR_CUDA = 2
+BM_ERR_DEVICE = 3
+
+BM_F32 = 0
+BM_BF16 = 1
+
+BM_DEVERR_BAD_ID = 0x1
+BM_DEVERR_BAD_POSITION = 0x2
+BM_DEVERR_BAD_SEQUENCE = 0x4
+
+# name -> (restype, argtypes). Every symbol include/bm_layer_ops.h declares.
+SIGNATURES = {
+    "bm_status_string": (c_char_p, [c_int]),
+    "bm_abi_version": (c_int, []),
+    "bm_last_error_message": (c_char_p, []),
+    "bm_status_read": (c_int, [c_void_p, P_INT32, c_void_p]),
+    "bm_embed_gather": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int,
+                                c_void_p, c_void_p]),
+    "bm_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float, c_int64, c_int64, c_int,
+                           c_void_p]),
+    "bm_add_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float, c_int,
+                               c_void_p]),
+    "bm_add": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p]),
+    "bm_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p]),
+    "bm_rope_table_fill": (c_int, [c_void_p, c_int32, c_int32, c_double, c_void_p]),
+    "bm_rope_table_create": (c_int, [c_int32, c_int32, c_double, ctypes.POINTER(c_void_p)]),
+    "bm_rope_table_destroy": (c_int, [c_void_p]),
+    "bm_rope_kv_store": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_void_p,
+                                 c_void_p, c_int32, c_double, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32,
+                                 c_int, c_void_p, c_void_p]),
+    "bm_rope": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_double, c_int64, c_int32,
+                        c_int32, c_int32, c_int, c_void_p, c_void_p]),
+    "bm_kv_store": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_int64, c_int32, c_int32, c_int32,
+                            c_int32, c_int, c_void_p, c_void_p]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class BMError(RuntimeError):
+    """A non-zero bm_status_t from the C ABI, with the library's message."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{message} [{status_name(status)}]")
+        self.status = status
+
+
+def status_name(status: int) -> str:
+    return {BM_OK: "BM_OK", BM_ERR_INVALID_ARGUMENT: "BM_ERR_INVALID_ARGUMENT", BM_ERR_CUDA: "BM_ERR_CUDA",
+            BM_ERR_DEVICE: "BM_ERR_DEVICE"}.get(status, f"BM_ERR_{status}")
+
+
+def lib_path() -> str:
+    return LIB_PATH
+
+
+def load() -> ctypes.CDLL:
+    """Loads the library once; raises if it is missing (no fallback path)."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"{LIB_PATH} is missing: build the sm_100a kernels first "
+                    "(python -m baremetalinferenceengine_b200.build)")
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, (restype, argtypes) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = restype
+                fn.argtypes = argtypes
+            _lib = lib
+        return _lib
+
+
+def check(status: int) -> None:
+    if status != BM_OK:
+        msg = load().bm_last_error_message()
+        raise BMError(status, msg.decode() if msg else "")

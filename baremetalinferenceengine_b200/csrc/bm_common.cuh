@@ -1,0 +1,132 @@
+// Device helpers shared by the layer-op kernels: element types, 16-byte vector
+// loads/stores with cache hints, warp reductions and device status bits.
+//
+// Every kernel computes in fp32. Storage is fp32 or bf16; a bf16 value widens to
+// fp32 exactly (a 16-bit shift) and narrows with round-to-nearest-even.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "bm_layer_ops.h"
+
+namespace bm {
+
+using bf16 = __nv_bfloat16;
+
+// Elements of T in one 16-byte vector.
+template <typename T>
+struct VecWidth;
+template <>
+struct VecWidth<float> {
+  static constexpr int value = 4;
+};
+template <>
+struct VecWidth<bf16> {
+  static constexpr int value = 8;
+};
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// Two fp32 values to one word of two bf16 (lo in the low half), RNE.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&b);
+}
+
+// 16 bytes of T -> VecWidth<T> floats.
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4& v, float* f) {
+  if constexpr (sizeof(T) == 4) {
+    f[0] = __uint_as_float(v.x);
+    f[1] = __uint_as_float(v.y);
+    f[2] = __uint_as_float(v.z);
+    f[3] = __uint_as_float(v.w);
+  } else {
+    f[0] = bf16_lo(v.x);
+    f[1] = bf16_hi(v.x);
+    f[2] = bf16_lo(v.y);
+    f[3] = bf16_hi(v.y);
+    f[4] = bf16_lo(v.z);
+    f[5] = bf16_hi(v.z);
+    f[6] = bf16_lo(v.w);
+    f[7] = bf16_hi(v.w);
+  }
+}
+
+// VecWidth<T> floats -> 16 bytes of T.
+template <typename T>
+__device__ __forceinline__ uint4 pack16(const float* f) {
+  uint4 v;
+  if constexpr (sizeof(T) == 4) {
+    v.x = __float_as_uint(f[0]);
+    v.y = __float_as_uint(f[1]);
+    v.z = __float_as_uint(f[2]);
+    v.w = __float_as_uint(f[3]);
+  } else {
+    v.x = pack_bf16x2(f[0], f[1]);
+    v.y = pack_bf16x2(f[2], f[3]);
+    v.z = pack_bf16x2(f[4], f[5]);
+    v.w = pack_bf16x2(f[6], f[7]);
+  }
+  return v;
+}
+
+// Rounds an fp32 value to the storage type and back (the value a store keeps).
+template <typename T>
+__device__ __forceinline__ float round_to(float x) {
+  if constexpr (sizeof(T) == 4) {
+    return x;
+  } else {
+    return __bfloat162float(__float2bfloat16_rn(x));
+  }
+}
+
+// Scalar element access.
+template <typename T>
+__device__ __forceinline__ float load1(const T* p) {
+  if constexpr (sizeof(T) == 4) {
+    return *reinterpret_cast<const float*>(p);
+  } else {
+    return __bfloat162float(*p);
+  }
+}
+template <typename T>
+__device__ __forceinline__ void store1(T* p, float x) {
+  if constexpr (sizeof(T) == 4) {
+    *reinterpret_cast<float*>(p) = x;
+  } else {
+    *p = __float2bfloat16_rn(x);
+  }
+}
+
+// Streaming 16-byte load: read once, evict first (ld.global.cs). Coherent, so
+// safe on buffers the same kernel writes (in-place ops).
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  return __ldcs(reinterpret_cast<const uint4*>(p));
+}
+// Read-only 16-byte load that should stay cached (weights, tables).
+__device__ __forceinline__ uint4 ld_keep(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+__device__ __forceinline__ void st_plain(void* p, const uint4& v) {
+  *reinterpret_cast<uint4*>(p) = v;
+}
+__device__ __forceinline__ void st_stream(void* p, const uint4& v) {
+  __stcs(reinterpret_cast<uint4*>(p), v);
+}
+
+// Butterfly sum: every lane of the warp gets the total.
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+__device__ __forceinline__ void raise_status(int32_t* status, int32_t bits) {
+  if (status != nullptr) atomicOr(status, bits);
+}
+
+}  // namespace bm

@@ -1,0 +1,443 @@
+// RoPE on Q and K with the K/V write into a static KV cache, for many tokens.
+//
+// Reference semantics:
+//   rope_kernel (src/kernels.cu:126-140): for one token at seq_pos, each pair
+//     (x[i], x[i + hd/2]) of every head is rotated by
+//     angle = seq_pos / theta^(2i/hd):  x[i] <- x[i] c - x[i+hd/2] s,
+//     x[i+hd/2] <- x[i+hd/2] c + x[i] s. launch_rope runs it on q, then on k.
+//   kv_store_kernel (src/kernels.cu:211-217):
+//     cache[(h * max_seq + pos) * hd + d] = src[h * hd + d].
+//   ExecutionEngine::run_layers calls rope, then kv_store for k and for v
+//   (src/execution_engine.cu:113-115): four launches per token per layer.
+//
+// Here one launch covers all tokens and, in the fused mode, does all three
+// steps: a block takes one token (grid-stride over tokens), stages that token's
+// (cos, sin) row in shared memory — from the position-keyed fp32 table, or
+// computed in fp64 when no table is given — and splits the token's work into
+// units: a Q pair unit rotates VEC elements from each half of one head in place,
+// a K pair unit rotates one K head's VEC pairs straight into k_cache, and a V
+// unit copies VEC elements into v_cache. Each thread issues the loads of up to
+// UPT units before the table barrier, so HBM latency overlaps the staging.
+// The cache layout is [num_seqs][num_kv_heads][max_seq][head_dim]
+// (include/kv_cache.h:37-40, with the batch dimension used).
+//
+// The (cos, sin) table is computed on the device in fp64 with CUDA's pow and
+// sincos, following the reference's CPU check loop (tests/kernel_tests.cu:180),
+// and rounded once to fp32. Rotation arithmetic is fp32.
+#include <algorithm>
+
+#include "bm_common.cuh"
+#include "bm_host.h"
+
+namespace bm {
+namespace {
+
+constexpr int kMaxHalf = 512;  // head_dim <= 1024
+constexpr int kUPT = 4;        // units whose loads a thread issues up front
+
+enum Mode { kFused = 0, kRope = 1, kStore = 2 };
+
+struct RopeArgs {
+  void* q;                    // [rows][hq][hd]
+  void* k;                    // [rows][hkv][hd]
+  const void* v;              // [rows][hkv][hd] (kFused: v; kStore: src)
+  const int32_t* positions;   // NULL: pos0 + row
+  const int32_t* seq_ids;     // NULL: 0
+  void* k_cache;              // [num_seqs][hkv][max_seq][hd]
+  void* v_cache;              // kStore: the destination cache
+  const float2* table;        // [table_len][half] or NULL
+  double theta;
+  int64_t rows;
+  int32_t pos0;
+  int32_t table_len;
+  int hq, hkv, hd, half, max_seq, num_seqs;
+  int upv;                    // pair units per head (half / VEC)
+  int cpv;                    // copy units per head (hd / VEC)
+  int q_units, k_units, total_units;
+  int32_t* status;
+};
+
+// VEC consecutive elements of T, held between load and store.
+template <typename T, int VEC>
+struct Chunk {
+  static_assert(VEC * sizeof(T) == 16, "vector chunks are 16 bytes");
+  uint4 raw;
+  __device__ __forceinline__ void load(const T* p) { raw = ld_stream(p); }
+  __device__ __forceinline__ void store(T* p) const { st_plain(p, raw); }
+  __device__ __forceinline__ void get(float* f) const { unpack16<T>(raw, f); }
+  __device__ __forceinline__ void set(const float* f) { raw = pack16<T>(f); }
+};
+template <typename T>
+struct Chunk<T, 1> {
+  float x;
+  __device__ __forceinline__ void load(const T* p) { x = load1<T>(p); }
+  __device__ __forceinline__ void store(T* p) const { store1<T>(p, x); }
+  __device__ __forceinline__ void get(float* f) const { f[0] = x; }
+  __device__ __forceinline__ void set(const float* f) { x = f[0]; }
+};
+
+// Where unit u of a token lives: kind 0 = Q pair, 1 = K pair, 2 = V copy;
+// head h and chunk c within the head.
+struct Unit {
+  int kind, h, c;
+};
+
+__device__ __forceinline__ Unit decode(const RopeArgs& a, int u) {
+  Unit r;
+  if (u < a.q_units) {
+    r.kind = 0;
+    r.h = u / a.upv;
+    r.c = u - r.h * a.upv;
+  } else if (u < a.q_units + a.k_units) {
+    u -= a.q_units;
+    r.kind = 1;
+    r.h = u / a.upv;
+    r.c = u - r.h * a.upv;
+  } else {
+    u -= a.q_units + a.k_units;
+    r.kind = 2;
+    r.h = u / a.cpv;
+    r.c = u - r.h * a.cpv;
+  }
+  return r;
+}
+
+template <typename T, int VEC, int MODE>
+__device__ __forceinline__ void load_unit(const RopeArgs& a, const Unit& u, int64_t row, Chunk<T, VEC>& c1,
+                                          Chunk<T, VEC>& c2) {
+  if (u.kind == 0) {
+    const T* base = static_cast<const T*>(a.q) + (row * a.hq + u.h) * a.hd + u.c * VEC;
+    c1.load(base);
+    c2.load(base + a.half);
+  } else if (u.kind == 1) {
+    const T* base = static_cast<const T*>(a.k) + (row * a.hkv + u.h) * a.hd + u.c * VEC;
+    c1.load(base);
+    c2.load(base + a.half);
+  } else {
+    const T* base = static_cast<const T*>(a.v) + (row * a.hkv + u.h) * a.hd + u.c * VEC;
+    c1.load(base);
+  }
+}
+
+template <typename T, int VEC, int MODE>
+__device__ __forceinline__ void finish_unit(const RopeArgs& a, const Unit& u, int64_t row, int64_t cache_base,
+                                            int64_t cache_head_stride, const float2* cs, Chunk<T, VEC>& c1,
+                                            Chunk<T, VEC>& c2) {
+  if (u.kind == 2) {
+    // V (kFused) or src (kStore): plain copy into the cache.
+    T* dst = static_cast<T*>(a.v_cache) + cache_base + u.h * cache_head_stride + u.c * VEC;
+    c1.store(dst);
+    return;
+  }
+  float x1[VEC], x2[VEC];
+  c1.get(x1);
+  c2.get(x2);
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) {
+    const float2 t = cs[u.c * VEC + e];  // (cos, sin)
+    const float first = x1[e], second = x2[e];
+    x1[e] = first * t.x - second * t.y;
+    x2[e] = second * t.x + first * t.y;
+  }
+  c1.set(x1);
+  c2.set(x2);
+  T* dst;
+  if (u.kind == 0) {
+    dst = static_cast<T*>(a.q) + (row * a.hq + u.h) * a.hd + u.c * VEC;
+  } else if (MODE == kFused) {
+    dst = static_cast<T*>(a.k_cache) + cache_base + u.h * cache_head_stride + u.c * VEC;
+  } else {
+    dst = static_cast<T*>(a.k) + (row * a.hkv + u.h) * a.hd + u.c * VEC;
+  }
+  c1.store(dst);
+  c2.store(dst + a.half);
+}
+
+template <typename T, int VEC, int MODE>
+__global__ void __launch_bounds__(256) rope_kv_kernel(RopeArgs a) {
+  __shared__ float2 cs[kMaxHalf];
+  const int tid = threadIdx.x;
+  const int nthreads = blockDim.x;
+  const int64_t cache_head_stride = static_cast<int64_t>(a.max_seq) * a.hd;
+
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const int32_t pos = a.positions ? a.positions[row] : static_cast<int32_t>(a.pos0 + row);
+    const int32_t seq = a.seq_ids ? a.seq_ids[row] : 0;
+    int32_t bad = 0;
+    if (pos < 0) bad |= BM_DEVERR_BAD_POSITION;
+    if (MODE != kRope) {
+      if (pos >= a.max_seq) bad |= BM_DEVERR_BAD_POSITION;
+      if (seq < 0 || seq >= a.num_seqs) bad |= BM_DEVERR_BAD_SEQUENCE;
+    }
+    if (MODE != kStore && a.table != nullptr && pos >= a.table_len) bad |= BM_DEVERR_BAD_POSITION;
+    if (bad) {  // uniform across the block: every thread read the same row
+      if (tid == 0) raise_status(a.status, bad);
+      continue;
+    }
+    const int64_t cache_base =
+        MODE == kRope ? 0 : (static_cast<int64_t>(seq) * a.hkv * a.max_seq + pos) * a.hd;
+
+    // Issue this thread's first UPT units' loads before the table barrier.
+    Chunk<T, VEC> c1[kUPT], c2[kUPT];
+#pragma unroll
+    for (int j = 0; j < kUPT; ++j) {
+      const int u = tid + j * nthreads;
+      if (u < a.total_units) load_unit<T, VEC, MODE>(a, decode(a, u), row, c1[j], c2[j]);
+    }
+
+    if (MODE != kStore) {
+      for (int i = tid; i < a.half; i += nthreads) {
+        float2 t;
+        if (a.table != nullptr) {
+          t = __ldg(a.table + static_cast<int64_t>(pos) * a.half + i);
+        } else {
+          const double angle = static_cast<double>(pos) / pow(a.theta, 2.0 * i / a.hd);
+          double s, c;
+          sincos(angle, &s, &c);
+          t = make_float2(static_cast<float>(c), static_cast<float>(s));
+        }
+        cs[i] = t;
+      }
+      __syncthreads();
+    }
+
+#pragma unroll
+    for (int j = 0; j < kUPT; ++j) {
+      const int u = tid + j * nthreads;
+      if (u < a.total_units) {
+        finish_unit<T, VEC, MODE>(a, decode(a, u), row, cache_base, cache_head_stride, cs, c1[j], c2[j]);
+      }
+    }
+    // Units beyond the first UPT per thread (very wide tokens).
+    for (int u = tid + kUPT * nthreads; u < a.total_units; u += nthreads) {
+      Chunk<T, VEC> d1, d2;
+      const Unit un = decode(a, u);
+      load_unit<T, VEC, MODE>(a, un, row, d1, d2);
+      finish_unit<T, VEC, MODE>(a, un, row, cache_base, cache_head_stride, cs, d1, d2);
+    }
+    if (MODE != kStore) __syncthreads();  // cs is restaged for the next token
+  }
+}
+
+__global__ void rope_table_kernel(float2* table, int32_t max_pos, int half, int hd, double theta) {
+  const int64_t n = static_cast<int64_t>(max_pos) * half;
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < n;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t p = idx / half;
+    const int i = static_cast<int>(idx - p * half);
+    const double angle = static_cast<double>(p) / pow(theta, 2.0 * i / hd);
+    double s, c;
+    sincos(angle, &s, &c);
+    table[idx] = make_float2(static_cast<float>(c), static_cast<float>(s));
+  }
+}
+
+template <typename T, int VEC, int MODE>
+int launch_typed(const RopeArgs& a, cudaStream_t stream, const char* what) {
+  const int want = (a.total_units + kUPT - 1) / kUPT;
+  const int block = std::min(256, std::max(64, (want + 31) / 32 * 32));
+  const int64_t cap = static_cast<int64_t>(sm_count()) * (2048 / block);
+  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min(a.rows, cap)));
+  rope_kv_kernel<T, VEC, MODE><<<grid, block, 0, stream>>>(a);
+  return check_launch(what);
+}
+
+template <int MODE>
+int launch(RopeArgs a, bm_dtype_t dtype, cudaStream_t stream, const char* what) {
+  const int es = dtype_size(dtype);
+  const int vec = 16 / es;
+  // Both halves of a pair (or a whole head when only copying) split into VEC-element chunks.
+  bool vec_ok = (MODE == kStore ? a.hd : a.half) % vec == 0;
+  for (const void* p : {static_cast<const void*>(a.q), static_cast<const void*>(a.k), a.v,
+                        static_cast<const void*>(a.k_cache), static_cast<const void*>(a.v_cache)}) {
+    if (p != nullptr && !aligned16(p)) vec_ok = false;
+  }
+  const int v_used = vec_ok ? vec : 1;
+  a.upv = a.half / v_used;
+  a.cpv = a.hd / v_used;
+  if (MODE == kStore) {
+    a.q_units = 0;
+    a.k_units = 0;
+    a.total_units = a.hkv * a.cpv;
+  } else {
+    a.q_units = a.hq * a.upv;
+    a.k_units = a.hkv * a.upv;
+    a.total_units = a.q_units + a.k_units + (MODE == kFused ? a.hkv * a.cpv : 0);
+  }
+  if (a.total_units == 0) return BM_OK;
+  if (dtype == BM_F32) {
+    return vec_ok ? launch_typed<float, 4, MODE>(a, stream, what) : launch_typed<float, 1, MODE>(a, stream, what);
+  }
+  return vec_ok ? launch_typed<bf16, 8, MODE>(a, stream, what) : launch_typed<bf16, 1, MODE>(a, stream, what);
+}
+
+int check_common(const char* what, int64_t rows, int hd, bm_dtype_t dtype) {
+  if (!valid_dtype(dtype)) return fail(BM_ERR_INVALID_ARGUMENT, "%s: bad dtype %d", what, static_cast<int>(dtype));
+  if (rows < 0) return fail(BM_ERR_INVALID_ARGUMENT, "%s: negative rows", what);
+  if (hd <= 0 || hd > 2 * kMaxHalf) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: head_dim %d outside [1, %d]", what, hd, 2 * kMaxHalf);
+  }
+  return BM_OK;
+}
+
+int check_table(const char* what, const void* table, int32_t table_len, double theta) {
+  if (table != nullptr) {
+    if (table_len <= 0) return fail(BM_ERR_INVALID_ARGUMENT, "%s: table_len must be > 0", what);
+    if ((reinterpret_cast<uintptr_t>(table) & 7u) != 0) return fail(BM_ERR_INVALID_ARGUMENT, "%s: table not 8-byte aligned", what);
+  } else if (!(theta > 0.0)) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: theta must be > 0 without a table", what);
+  }
+  return BM_OK;
+}
+
+}  // namespace
+}  // namespace bm
+
+extern "C" int bm_rope_kv_store(void* q, const void* k, const void* v, const int32_t* positions, int32_t pos0,
+                                const int32_t* seq_ids, void* k_cache, void* v_cache, const void* rope_table,
+                                int32_t table_len, double theta, int64_t rows, int32_t num_q_heads,
+                                int32_t num_kv_heads, int32_t head_dim, int32_t max_seq, int32_t num_seqs,
+                                bm_dtype_t dtype, int32_t* d_status, void* stream) {
+  using namespace bm;
+  const char* what = "bm_rope_kv_store";
+  if (int st = check_common(what, rows, head_dim, dtype)) return st;
+  if (head_dim % 2) return fail(BM_ERR_INVALID_ARGUMENT, "%s: head_dim must be even", what);
+  if (num_q_heads < 0 || num_kv_heads < 0 || max_seq <= 0 || num_seqs <= 0) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: bad head counts, max_seq or num_seqs", what);
+  }
+  if (int st = check_table(what, rope_table, table_len, theta)) return st;
+  if (rows == 0 || (num_q_heads == 0 && num_kv_heads == 0)) return BM_OK;
+  if ((num_q_heads > 0 && !q) || (num_kv_heads > 0 && (!k || !v || !k_cache || !v_cache))) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: NULL pointer", what);
+  }
+  if (!positions && (pos0 < 0 || static_cast<int64_t>(pos0) + rows > max_seq)) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: positions pos0..pos0+rows-1 outside [0, max_seq)", what);
+  }
+  RopeArgs a{};
+  a.q = q;
+  a.k = const_cast<void*>(k);
+  a.v = v;
+  a.positions = positions;
+  a.pos0 = pos0;
+  a.seq_ids = seq_ids;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.table = static_cast<const float2*>(rope_table);
+  a.table_len = table_len;
+  a.theta = theta;
+  a.rows = rows;
+  a.hq = num_q_heads;
+  a.hkv = num_kv_heads;
+  a.hd = head_dim;
+  a.half = head_dim / 2;
+  a.max_seq = max_seq;
+  a.num_seqs = num_seqs;
+  a.status = d_status;
+  return launch<kFused>(a, dtype, as_stream(stream), what);
+}
+
+extern "C" int bm_rope(void* q, void* k, const int32_t* positions, int32_t pos0, const void* rope_table,
+                       int32_t table_len, double theta, int64_t rows, int32_t num_q_heads, int32_t num_kv_heads,
+                       int32_t head_dim, bm_dtype_t dtype, int32_t* d_status, void* stream) {
+  using namespace bm;
+  const char* what = "bm_rope";
+  if (int st = check_common(what, rows, head_dim, dtype)) return st;
+  if (head_dim % 2) return fail(BM_ERR_INVALID_ARGUMENT, "%s: head_dim must be even", what);
+  if (num_q_heads < 0 || num_kv_heads < 0) return fail(BM_ERR_INVALID_ARGUMENT, "%s: negative head count", what);
+  if (int st = check_table(what, rope_table, table_len, theta)) return st;
+  if (rows == 0 || (num_q_heads == 0 && num_kv_heads == 0)) return BM_OK;
+  if ((num_q_heads > 0 && !q) || (num_kv_heads > 0 && !k)) return fail(BM_ERR_INVALID_ARGUMENT, "%s: NULL pointer", what);
+  if (!positions && pos0 < 0) return fail(BM_ERR_INVALID_ARGUMENT, "%s: negative position", what);
+  RopeArgs a{};
+  a.q = q;
+  a.k = k;
+  a.positions = positions;
+  a.pos0 = pos0;
+  a.table = static_cast<const float2*>(rope_table);
+  a.table_len = table_len;
+  a.theta = theta;
+  a.rows = rows;
+  a.hq = num_q_heads;
+  a.hkv = num_kv_heads;
+  a.hd = head_dim;
+  a.half = head_dim / 2;
+  a.max_seq = 1;
+  a.num_seqs = 1;
+  a.status = d_status;
+  return launch<kRope>(a, dtype, as_stream(stream), what);
+}
+
+extern "C" int bm_kv_store(void* cache, const void* src, const int32_t* positions, int32_t pos0,
+                           const int32_t* seq_ids, int64_t rows, int32_t num_heads, int32_t head_dim,
+                           int32_t max_seq, int32_t num_seqs, bm_dtype_t dtype, int32_t* d_status, void* stream) {
+  using namespace bm;
+  const char* what = "bm_kv_store";
+  if (int st = check_common(what, rows, head_dim, dtype)) return st;
+  if (num_heads < 0 || max_seq <= 0 || num_seqs <= 0) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: bad num_heads, max_seq or num_seqs", what);
+  }
+  if (rows == 0 || num_heads == 0) return BM_OK;
+  if (!cache || !src) return fail(BM_ERR_INVALID_ARGUMENT, "%s: NULL pointer", what);
+  if (!positions && (pos0 < 0 || static_cast<int64_t>(pos0) + rows > max_seq)) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: positions pos0..pos0+rows-1 outside [0, max_seq)", what);
+  }
+  RopeArgs a{};
+  a.v = src;
+  a.v_cache = cache;
+  a.positions = positions;
+  a.pos0 = pos0;
+  a.seq_ids = seq_ids;
+  a.rows = rows;
+  a.hkv = num_heads;
+  a.hd = head_dim;
+  a.half = head_dim / 2;
+  a.max_seq = max_seq;
+  a.num_seqs = num_seqs;
+  a.status = d_status;
+  return launch<kStore>(a, dtype, as_stream(stream), what);
+}
+
+extern "C" int bm_rope_table_fill(void* table, int32_t max_pos, int32_t head_dim, double theta, void* stream) {
+  using namespace bm;
+  const char* what = "bm_rope_table_fill";
+  if (max_pos <= 0 || head_dim <= 0 || head_dim % 2 || !(theta > 0.0)) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: need max_pos > 0, even head_dim > 0, theta > 0", what);
+  }
+  if (!table || (reinterpret_cast<uintptr_t>(table) & 7u)) return fail(BM_ERR_INVALID_ARGUMENT, "%s: bad table pointer", what);
+  const int half = head_dim / 2;
+  const int64_t n = static_cast<int64_t>(max_pos) * half;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, static_cast<int64_t>(sm_count()) * 8));
+  rope_table_kernel<<<grid, 256, 0, as_stream(stream)>>>(static_cast<float2*>(table), max_pos, half, head_dim, theta);
+  return check_launch(what);
+}
+
+extern "C" int bm_rope_table_create(int32_t max_pos, int32_t head_dim, double theta, void** table_out) {
+  using namespace bm;
+  if (!table_out) return fail(BM_ERR_INVALID_ARGUMENT, "bm_rope_table_create: NULL table_out");
+  *table_out = nullptr;
+  if (max_pos <= 0 || head_dim <= 0 || head_dim % 2 || !(theta > 0.0)) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "bm_rope_table_create: need max_pos > 0, even head_dim > 0, theta > 0");
+  }
+  void* p = nullptr;
+  const size_t bytes = static_cast<size_t>(max_pos) * head_dim / 2 * sizeof(float2);
+  cudaError_t err = cudaMalloc(&p, bytes);
+  if (err != cudaSuccess) return fail(BM_ERR_CUDA, "bm_rope_table_create: cudaMalloc: %s", cudaGetErrorString(err));
+  int st = bm_rope_table_fill(p, max_pos, head_dim, theta, nullptr);
+  if (st == BM_OK) {
+    err = cudaStreamSynchronize(nullptr);
+    if (err != cudaSuccess) st = fail(BM_ERR_CUDA, "bm_rope_table_create: %s", cudaGetErrorString(err));
+  }
+  if (st != BM_OK) {
+    cudaFree(p);
+    return st;
+  }
+  *table_out = p;
+  return BM_OK;
+}
+
+extern "C" int bm_rope_table_destroy(void* table) {
+  if (table == nullptr) return BM_OK;
+  cudaError_t err = cudaFree(table);
+  if (err != cudaSuccess) return bm::fail(BM_ERR_CUDA, "bm_rope_table_destroy: %s", cudaGetErrorString(err));
+  return BM_OK;
+}

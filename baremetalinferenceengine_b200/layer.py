@@ -1,0 +1,191 @@
+"""One layer's memory-bound ops over a batch of tokens ("a layer step").
+
+The in-scope half of ExecutionEngine::run_layers (src/execution_engine.cu:89-128),
+batched over rows and with the adds fused into the norms that follow them:
+
+    hidden        = embed[ids]                                  (:98-99)
+    hidden       += attn_out;  y_attn = rmsnorm(hidden) * w_attn (:118 + :109/:121)
+    q             = rope(q); k_cache/v_cache[seq, :, pos] = rope(k), v   (:113-115)
+    hidden       += ffn_out;   y_ffn  = rmsnorm(hidden) * w_ffn  (:126 + :121/:80)
+    act           = silu(gate) * up                             (:124)
+
+The GEMMs between these ops are outside the path: their outputs (attn_out, q,
+k, v, ffn_out, gate, up) are inputs here. :data:`WORKLOADS` holds the token
+layouts and model shapes the kernels are measured on; :class:`LayerBuffers`
+allocates and seeds one step's device buffers; :func:`run_step` issues the five
+launches through the C ABI.
+"""
+from __future__ import annotations
+
+import dataclasses
+from typing import Optional
+
+import torch
+
+from . import ops
+
+
+@dataclasses.dataclass(frozen=True)
+class LayerShape:
+    name: str
+    rows: int          # tokens per step (per GPU)
+    dim: int
+    hq: int
+    hkv: int
+    hd: int
+    ffn: int
+    vocab: int
+    theta: float
+    max_seq: int
+    num_seqs: int
+    dtype: torch.dtype
+    eps: float = 1e-5
+    positions: str = "tiled"  # "tiled": pos = r mod max_seq, seq = r // max_seq; "uniform": pos ~ U[0, max_seq)
+    description: str = ""
+
+    @property
+    def es(self) -> int:
+        return 4 if self.dtype == torch.float32 else 2
+
+    def bytes_per_row(self) -> dict:
+        """Algorithmic HBM bytes per token for each kernel: every input element read
+        once and every output element written once (weights, the RoPE table and
+        the embedding rows' reuse are not counted)."""
+        es = self.es
+        return {
+            "embed_gather": 2 * self.dim * es + 4,
+            "add_rmsnorm": 4 * self.dim * es,  # read residual + delta, write residual + out
+            "rope_kv_store": (2 * self.hq * self.hd + 2 * self.hkv * self.hd + 2 * self.hkv * self.hd) * es + 8,
+            "swiglu": 3 * self.ffn * es,
+        }
+
+    def step_kernels(self) -> list:
+        """(kernel, algorithmic bytes per launch) in launch order for one step."""
+        b = self.bytes_per_row()
+        r = self.rows
+        return [("embed_gather", b["embed_gather"] * r), ("add_rmsnorm_attn", b["add_rmsnorm"] * r),
+                ("rope_kv_store", b["rope_kv_store"] * r), ("add_rmsnorm_ffn", b["add_rmsnorm"] * r),
+                ("swiglu", b["swiglu"] * r)]
+
+    def step_bytes(self) -> int:
+        return sum(n for _, n in self.step_kernels())
+
+    def with_rows(self, rows: int) -> "LayerShape":
+        return dataclasses.replace(self, rows=rows)
+
+
+# Synthetic workloads (seeded; no dataset): the model shapes and token layouts the
+# kernels are measured on.
+WORKLOADS = {
+    "tinyllama_fp32": LayerShape(
+        "tinyllama_fp32", rows=256, dim=288, hq=6, hkv=6, hd=48, ffn=768, vocab=32000, theta=1e4, max_seq=256,
+        num_seqs=1, dtype=torch.float32,
+        description="tinyllama-15M-shaped layer, fp32, 256 tokens at positions 0..255"),
+    "llama8b_decode_bf16": LayerShape(
+        "llama8b_decode_bf16", rows=64, dim=4096, hq=32, hkv=8, hd=128, ffn=14336, vocab=128256, theta=5e5,
+        max_seq=8192, num_seqs=64, dtype=torch.bfloat16, positions="uniform",
+        description="Llama-3-8B decode: 64 tokens of 64 sequences, positions U[0,8192)"),
+    "llama8b_decode_fp32": LayerShape(
+        "llama8b_decode_fp32", rows=64, dim=4096, hq=32, hkv=8, hd=128, ffn=14336, vocab=128256, theta=5e5,
+        max_seq=8192, num_seqs=64, dtype=torch.float32, positions="uniform",
+        description="Llama-3-8B decode, fp32"),
+    "llama8b_prefill_bf16": LayerShape(
+        "llama8b_prefill_bf16", rows=32768, dim=4096, hq=32, hkv=8, hd=128, ffn=14336, vocab=128256, theta=5e5,
+        max_seq=8192, num_seqs=4, dtype=torch.bfloat16,
+        description="Llama-3-8B prefill: 4 sequences x 8192 tokens"),
+    "llama70b_bf16": LayerShape(
+        "llama70b_bf16", rows=131072, dim=8192, hq=64, hkv=8, hd=128, ffn=28672, vocab=128256, theta=5e5,
+        max_seq=8192, num_seqs=16, dtype=torch.bfloat16,
+        description="Llama-3-70B: 131072 tokens = 16 sequences x 8192 positions"),
+}
+
+
+def _generator(device, seed: int) -> torch.Generator:
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    return g
+
+
+class LayerBuffers:
+    """Device buffers of one layer step, seeded N(0,1) activations, 1+N(0,0.02)
+    norm weights, N(0,0.02) embedding table, uniform token ids."""
+
+    def __init__(self, shape: LayerShape, device, seed: int = 0, row_offset: int = 0, with_table: bool = True):
+        s = shape
+        self.shape = s
+        self.device = torch.device(device)
+        dt = s.dtype
+        g = _generator(self.device, seed)
+
+        def randn(*size, scale=1.0, offset=0.0):
+            t = torch.randn(*size, generator=g, device=self.device, dtype=torch.float32)
+            if scale != 1.0:
+                t.mul_(scale)
+            if offset != 0.0:
+                t.add_(offset)
+            return t.to(dt)
+
+        R, D = s.rows, s.dim
+        self.embed = randn(s.vocab, D, scale=0.02)
+        self.ids = torch.randint(0, s.vocab, (R,), generator=g, device=self.device, dtype=torch.int32)
+        if s.positions == "uniform":
+            self.positions = torch.randint(0, s.max_seq, (R,), generator=g, device=self.device, dtype=torch.int32)
+            self.seq_ids = (torch.arange(R, device=self.device, dtype=torch.int32) % s.num_seqs).contiguous()
+        else:
+            glob = torch.arange(row_offset, row_offset + R, device=self.device, dtype=torch.int64)
+            self.positions = (glob % s.max_seq).to(torch.int32)
+            seq = glob // s.max_seq - row_offset // s.max_seq
+            self.seq_ids = (seq % s.num_seqs).to(torch.int32)
+        self.hidden = torch.empty(R, D, dtype=dt, device=self.device)
+        self.attn_out = randn(R, D)
+        self.w_attn = randn(D, scale=0.02, offset=1.0)
+        self.y_attn = torch.empty(R, D, dtype=dt, device=self.device)
+        self.q = randn(R, s.hq, s.hd)
+        self.k = randn(R, s.hkv, s.hd)
+        self.v = randn(R, s.hkv, s.hd)
+        self.k_cache = torch.zeros(s.num_seqs, s.hkv, s.max_seq, s.hd, dtype=dt, device=self.device)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        self.ffn_out = randn(R, D)
+        self.w_ffn = randn(D, scale=0.02, offset=1.0)
+        self.y_ffn = torch.empty(R, D, dtype=dt, device=self.device)
+        self.gate = randn(R, s.ffn)
+        self.up = randn(R, s.ffn)
+        self.act = torch.empty(R, s.ffn, dtype=dt, device=self.device)
+        self.table = ops.RopeTable(s.max_seq, s.hd, s.theta, self.device) if with_table else None
+        self.status = ops.DeviceStatus(self.device)
+
+    # tensors a host-buffer (end-to-end) call copies in and out each step
+    INPUTS = ("ids", "positions", "seq_ids", "attn_out", "q", "k", "v", "ffn_out", "gate", "up")
+    OUTPUTS = ("hidden", "y_attn", "q", "y_ffn", "act")
+
+    def nbytes(self, names) -> int:
+        return sum(getattr(self, n).numel() * getattr(self, n).element_size() for n in names)
+
+
+def run_step(b: LayerBuffers, stream: Optional[torch.cuda.Stream] = None, events: Optional[list] = None,
+             rows: Optional[slice] = None) -> int:
+    """Issues the step's five kernels on `stream` (default: the current stream).
+    With `events` (6 CUDA events), records one before the first and after each
+    launch. `rows` restricts the step to a contiguous row range (a chunk).
+    Returns the number of kernel launches."""
+    s = b.shape
+    sl = rows if rows is not None else slice(0, s.rows)
+
+    def rec(i):
+        if events is not None:
+            events[i].record(stream)
+
+    st = b.status
+    rec(0)
+    ops.embed_gather(b.embed, b.ids[sl], out=b.hidden[sl], status=st, stream=stream)
+    rec(1)
+    ops.add_rmsnorm(b.hidden[sl], b.attn_out[sl], b.w_attn, s.eps, out=b.y_attn[sl], stream=stream)
+    rec(2)
+    ops.rope_kv_store(b.q[sl], b.k[sl], b.v[sl], b.positions[sl], b.k_cache, b.v_cache, table=b.table,
+                      theta=s.theta, seq_ids=b.seq_ids[sl], status=st, stream=stream)
+    rec(3)
+    ops.add_rmsnorm(b.hidden[sl], b.ffn_out[sl], b.w_ffn, s.eps, out=b.y_ffn[sl], stream=stream)
+    rec(4)
+    ops.swiglu(b.gate[sl], b.up[sl], out=b.act[sl], stream=stream)
+    rec(5)
+    return 5

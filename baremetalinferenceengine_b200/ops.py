@@ -1,0 +1,304 @@
+"""Host-side API over the C ABI, on torch CUDA tensors (torch provides device
+memory and streams; every op runs in ``libbm_layer_ops.so``).
+
+Two layers, mirroring the reference:
+
+* ``launch_*`` — the reference's single-token fp32 launch functions
+  (include/kernels.cuh:9,15,29,32,36) with the same names, argument order and
+  meaning; tensors stand in for the raw device pointers. Where the reference
+  exits the process through CUDA_CHECK, these raise :class:`BMError`.
+* batched ops — ``embed_gather``, ``rmsnorm``, ``add_rmsnorm``, ``swiglu``,
+  ``add``, ``rope``, ``rope_kv_store``, ``kv_store`` over many rows, fp32 or
+  bf16, on the current torch stream of the tensors' device.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import BMError, check, load  # noqa: F401  (re-exported)
+
+_DTYPES = {torch.float32: _lib.BM_F32, torch.bfloat16: _lib.BM_BF16}
+
+
+def bm_dtype(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, f"unsupported dtype {t.dtype} (float32 or bfloat16)") from None
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "tensor is not on a CUDA device")
+    return t.data_ptr()
+
+
+def _dev(t: torch.Tensor) -> torch.device:
+    """The tensor's CUDA device; a CPU tensor is an argument error (no CPU path)."""
+    if not t.is_cuda:
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "tensor is not on a CUDA device")
+    return t.device
+
+
+def _stream(device: torch.device, stream: Optional[torch.cuda.Stream]) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream(device)
+    return s.cuda_stream
+
+
+def _dense(t: torch.Tensor, name: str) -> None:
+    if not t.is_contiguous():
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, f"{name} must be contiguous")
+
+
+def _same(ref: torch.Tensor, *others: Optional[torch.Tensor]) -> None:
+    for o in others:
+        if o is not None and (o.device != ref.device or o.dtype != ref.dtype):
+            raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "tensors must share device and dtype")
+
+
+def _i32(t: Optional[torch.Tensor], name: str) -> None:
+    if t is not None and (t.dtype != torch.int32 or not t.is_contiguous() or not t.is_cuda):
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, f"{name} must be a contiguous int32 CUDA tensor")
+
+
+class DeviceStatus:
+    """One int32 device word that kernels OR ``BM_DEVERR_*`` bits into."""
+
+    def __init__(self, device: torch.device | str | int = "cuda"):
+        self.word = torch.zeros(1, dtype=torch.int32, device=device)
+
+    @property
+    def ptr(self) -> int:
+        return self.word.data_ptr()
+
+    def read(self, stream: Optional[torch.cuda.Stream] = None) -> int:
+        """Synchronises the stream, returns the bits and clears the word."""
+        flags = ctypes.c_int32(0)
+        with torch.cuda.device(self.word.device):
+            st = load().bm_status_read(self.ptr, ctypes.byref(flags), _stream(self.word.device, stream))
+        if st not in (_lib.BM_OK, _lib.BM_ERR_DEVICE):
+            check(st)
+        return int(flags.value)
+
+
+class RopeTable:
+    """Device (cos, sin) table [max_pos][head_dim/2] of fp32 pairs, filled in fp64."""
+
+    def __init__(self, max_pos: int, head_dim: int, theta: float, device: torch.device | str | int = "cuda",
+                 stream: Optional[torch.cuda.Stream] = None):
+        self.max_pos, self.head_dim, self.theta = int(max_pos), int(head_dim), float(theta)
+        self.data = torch.empty(self.max_pos, self.head_dim // 2, 2, dtype=torch.float32, device=device)
+        with torch.cuda.device(self.data.device):
+            check(load().bm_rope_table_fill(self.data.data_ptr(), self.max_pos, self.head_dim, self.theta,
+                                            _stream(self.data.device, stream)))
+
+    @property
+    def ptr(self) -> int:
+        return self.data.data_ptr()
+
+
+# --------------------------------------------------------------------------
+# Batched ops
+# --------------------------------------------------------------------------
+
+def embed_gather(table: torch.Tensor, ids: torch.Tensor, out: Optional[torch.Tensor] = None,
+                 status: Optional[DeviceStatus] = None, stream=None) -> torch.Tensor:
+    """out[r] = table[ids[r]] (bit-exact). Bad ids leave rows unwritten and set BAD_ID."""
+    _dense(table, "table")
+    _i32(ids, "ids")
+    rows, (vocab, dim) = ids.numel(), table.shape
+    if out is None:
+        out = torch.empty(rows, dim, dtype=table.dtype, device=table.device)
+    _same(table, out)
+    if out.dim() != 2 or out.shape[0] != rows or out.shape[1] != dim or out.stride(1) != 1:
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "out must be [rows, dim] with unit inner stride")
+    with torch.cuda.device(_dev(table)):
+        check(load().bm_embed_gather(_ptr(out), _ptr(table), _ptr(ids), rows, dim, vocab, out.stride(0),
+                                     bm_dtype(table), status.ptr if status else None,
+                                     _stream(table.device, stream)))
+    return out
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-5, out: Optional[torch.Tensor] = None,
+            stream=None) -> torch.Tensor:
+    """Row-wise RMSNorm of x [rows, dim]; ``out=x`` normalises in place."""
+    dim = x.shape[-1]
+    x2 = x.reshape(-1, dim) if x.is_contiguous() else x
+    if x2.dim() != 2 or x2.stride(1) != 1:
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "x must be [rows, dim] with unit inner stride")
+    if out is None:
+        out = torch.empty_like(x)
+    out2 = out.reshape(-1, dim) if out.is_contiguous() else out
+    _same(x, weight, out)
+    if weight.numel() != dim:
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "weight must have dim elements")
+    with torch.cuda.device(_dev(x)):
+        check(load().bm_rmsnorm(_ptr(out2), _ptr(x2), _ptr(weight), x2.shape[0], dim, eps, x2.stride(0),
+                                out2.stride(0), bm_dtype(x), _stream(x.device, stream)))
+    return out
+
+
+def add_rmsnorm(residual: torch.Tensor, delta: torch.Tensor, weight: torch.Tensor, eps: float = 1e-5,
+                out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """residual += delta (in place); returns rmsnorm(residual) * weight."""
+    for t, n in ((residual, "residual"), (delta, "delta")):
+        _dense(t, n)
+    if residual.shape != delta.shape:
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "residual and delta shapes differ")
+    dim = residual.shape[-1]
+    if out is None:
+        out = torch.empty_like(residual)
+    _dense(out, "out")
+    _same(residual, delta, weight, out)
+    with torch.cuda.device(_dev(residual)):
+        check(load().bm_add_rmsnorm(_ptr(residual), _ptr(delta), _ptr(weight), _ptr(out), residual.numel() // dim,
+                                    dim, eps, bm_dtype(residual), _stream(residual.device, stream)))
+    return out
+
+
+def swiglu(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """out = silu(gate) * up, element-wise."""
+    _dense(gate, "gate")
+    _dense(up, "up")
+    if out is None:
+        out = torch.empty_like(gate)
+    _dense(out, "out")
+    _same(gate, up, out)
+    if gate.numel() != up.numel() or out.numel() != gate.numel():
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "gate, up and out sizes differ")
+    with torch.cuda.device(_dev(gate)):
+        check(load().bm_swiglu(_ptr(out), _ptr(gate), _ptr(up), gate.numel(), bm_dtype(gate),
+                               _stream(gate.device, stream)))
+    return out
+
+
+def add(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """out = a + b, element-wise (out may be a or b)."""
+    _dense(a, "a")
+    _dense(b, "b")
+    if out is None:
+        out = torch.empty_like(a)
+    _dense(out, "out")
+    _same(a, b, out)
+    if a.numel() != b.numel() or out.numel() != a.numel():
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "a, b and out sizes differ")
+    with torch.cuda.device(_dev(a)):
+        check(load().bm_add(_ptr(out), _ptr(a), _ptr(b), a.numel(), bm_dtype(a), _stream(a.device, stream)))
+    return out
+
+
+def _positions(positions, rows):
+    if isinstance(positions, int):
+        return None, positions
+    _i32(positions, "positions")
+    if positions.numel() != rows:
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "positions must have one entry per row")
+    return positions, 0
+
+
+def rope_kv_store(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, positions, k_cache: torch.Tensor,
+                  v_cache: torch.Tensor, table: Optional[RopeTable] = None, theta: float = 10000.0,
+                  seq_ids: Optional[torch.Tensor] = None, status: Optional[DeviceStatus] = None,
+                  stream=None) -> None:
+    """Rotates q [rows, Hq, hd] in place; writes rotated k and raw v into the caches
+    [num_seqs, Hkv, max_seq, hd] at (seq_ids[r], positions[r]). ``positions`` is an
+    int32 tensor or an int pos0 (token r at pos0 + r)."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        _dense(t, n)
+    _same(q, k, v, k_cache, v_cache)
+    rows, hq, hd = q.shape[0], q.shape[1], q.shape[2]
+    hkv = k.shape[1]
+    num_seqs, max_seq = k_cache.shape[0], k_cache.shape[2]
+    if k.shape != v.shape or k.shape[0] != rows or k_cache.shape != v_cache.shape or k_cache.shape[1] != hkv:
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "q/k/v/cache shapes disagree")
+    pos_t, pos0 = _positions(positions, rows)
+    _i32(seq_ids, "seq_ids")
+    with torch.cuda.device(_dev(q)):
+        check(load().bm_rope_kv_store(_ptr(q), _ptr(k), _ptr(v), _ptr(pos_t), pos0, _ptr(seq_ids), _ptr(k_cache),
+                                      _ptr(v_cache), table.ptr if table else None,
+                                      table.max_pos if table else 0, theta, rows, hq, hkv, hd, max_seq, num_seqs,
+                                      bm_dtype(q), status.ptr if status else None, _stream(q.device, stream)))
+
+
+def rope(q: Optional[torch.Tensor], k: Optional[torch.Tensor], positions, table: Optional[RopeTable] = None,
+         theta: float = 10000.0, status: Optional[DeviceStatus] = None, stream=None) -> None:
+    """Rotates q [rows, Hq, hd] and k [rows, Hkv, hd] in place (either may be None)."""
+    ref = q if q is not None else k
+    for t, n in ((q, "q"), (k, "k")):
+        if t is not None:
+            _dense(t, n)
+    _same(ref, q, k)
+    rows, hd = ref.shape[0], ref.shape[2]
+    pos_t, pos0 = _positions(positions, rows)
+    with torch.cuda.device(_dev(ref)):
+        check(load().bm_rope(_ptr(q), _ptr(k), _ptr(pos_t), pos0, table.ptr if table else None,
+                             table.max_pos if table else 0, theta, rows, q.shape[1] if q is not None else 0,
+                             k.shape[1] if k is not None else 0, hd, bm_dtype(ref),
+                             status.ptr if status else None, _stream(ref.device, stream)))
+
+
+def kv_store(cache: torch.Tensor, src: torch.Tensor, positions, seq_ids: Optional[torch.Tensor] = None,
+             status: Optional[DeviceStatus] = None, stream=None) -> None:
+    """cache [num_seqs, H, max_seq, hd][seq_ids[r], :, positions[r]] = src [rows, H, hd][r]."""
+    _dense(cache, "cache")
+    _dense(src, "src")
+    _same(cache, src)
+    rows, h, hd = src.shape
+    pos_t, pos0 = _positions(positions, rows)
+    _i32(seq_ids, "seq_ids")
+    with torch.cuda.device(_dev(src)):
+        check(load().bm_kv_store(_ptr(cache), _ptr(src), _ptr(pos_t), pos0, _ptr(seq_ids), rows, h, hd,
+                                 cache.shape[2], cache.shape[0], bm_dtype(src), status.ptr if status else None,
+                                 _stream(src.device, stream)))
+
+
+# --------------------------------------------------------------------------
+# The reference's launch API (single token, fp32), include/kernels.cuh
+# --------------------------------------------------------------------------
+
+def _stream_arg(stream) -> int:
+    if stream is None or stream == 0:
+        return 0
+    return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+
+
+def launch_rms_norm(out: torch.Tensor, inp: torch.Tensor, weight: torch.Tensor, size: int, eps: float = 1e-5,
+                    stream=0) -> None:
+    """include/kernels.cuh:9 — one vector of ``size`` floats; out may be inp."""
+    with torch.cuda.device(_dev(inp)):
+        check(load().bm_rmsnorm(_ptr(out), _ptr(inp), _ptr(weight), 1, size, eps, size, size, _lib.BM_F32,
+                                _stream_arg(stream)))
+
+
+def launch_rope(q: torch.Tensor, k: torch.Tensor, seq_pos: int, head_dim: int, num_heads: int, num_kv_heads: int,
+                theta: float = 10000.0, stream=0) -> None:
+    """include/kernels.cuh:15 — rotates one token's q and k in place."""
+    with torch.cuda.device(_dev(q)):
+        check(load().bm_rope(_ptr(q), _ptr(k), None, seq_pos, None, 0, float(theta), 1, num_heads, num_kv_heads,
+                             head_dim, _lib.BM_F32, None, _stream_arg(stream)))
+
+
+def launch_swiglu(out: torch.Tensor, gate: torch.Tensor, up: torch.Tensor, size: int, stream=0) -> None:
+    """include/kernels.cuh:29 — out = silu(gate) * up."""
+    with torch.cuda.device(_dev(gate)):
+        check(load().bm_swiglu(_ptr(out), _ptr(gate), _ptr(up), size, _lib.BM_F32, _stream_arg(stream)))
+
+
+def launch_add(out: torch.Tensor, a: torch.Tensor, b: torch.Tensor, size: int, stream=0) -> None:
+    """include/kernels.cuh:32 — out = a + b; out may alias a or b."""
+    with torch.cuda.device(_dev(a)):
+        check(load().bm_add(_ptr(out), _ptr(a), _ptr(b), size, _lib.BM_F32, _stream_arg(stream)))
+
+
+def launch_kv_store(cache: torch.Tensor, src: torch.Tensor, seq_pos: int, num_heads: int, head_dim: int,
+                    max_seq_len: int, stream=0) -> None:
+    """include/kernels.cuh:36 — cache [H][max_seq][hd] at seq_pos = src [H][hd]."""
+    with torch.cuda.device(_dev(src)):
+        check(load().bm_kv_store(_ptr(cache), _ptr(src), None, seq_pos, None, 1, num_heads, head_dim, max_seq_len,
+                                 1, _lib.BM_F32, None, _stream_arg(stream)))

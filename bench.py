@@ -1,0 +1,505 @@
+#!/usr/bin/env python
+"""Throughput of the fused layer-op kernels on B200: one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload llama70b_bf16] [--rows R] [--e2e-steps E]
+
+A step is one layer's memory-bound ops over one batch of tokens, issued through
+the C ABI: embedding gather -> residual add + RMSNorm -> RoPE on Q/K with the
+K/V write into the static cache -> residual add + RMSNorm -> SwiGLU
+(baremetalinferenceengine_b200.layer). The default workload is the
+Llama-3-70B shape: 131072 tokens (16 sequences x 8192 positions), dim 8192,
+64 Q / 8 KV heads of 128, FFN 28672, bf16 — 49 GB of algorithmic traffic per
+step, far above the 126 MB L2, so no flush is needed between steps.
+
+N > 1 runs one process per GPU (torchrun); every rank owns its own batch of
+tokens (weak scaling: the job grows with N, rows are independent, no
+collectives on the data path). Time is the max over ranks of the CUDA-event
+time of exactly K steps, bracketed by a barrier and a synchronize.
+
+value: whole-job algorithmic HBM GB/s (bytes every kernel must move / time).
+e2e:   the same metric with the step's inputs copied in from pinned host memory
+       and its outputs copied back, every step, inside the timed region.
+--impl reference: the CPU implementation (the oracle: the reference's
+       double-precision check loops restated in C, pinned bit-for-bit to them)
+       on all host cores, over a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "achieved HBM GB/s and % of B200 peak per fused layer kernel; rows/s at 1/2/4/8 GPUs"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def parse_args():
+    from baremetalinferenceengine_b200.layer import WORKLOADS
+
+    ap = argparse.ArgumentParser(description="fused layer-op kernel benchmark")
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama70b_bf16")
+    ap.add_argument("--rows", type=int, default=0, help="override tokens per GPU")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-chunks", type=int, default=16)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU-baseline sample time")
+    return ap.parse_args()
+
+
+def measured_peak():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            peaks = json.load(f)
+        return float(peaks["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ----------------------------------------------------------------------------- clocks
+
+NVML_REASONS = {
+    0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+    0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting", 0x10: "sync_boost",
+}
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML (read-only) while running."""
+
+    def __init__(self, torch_device, period_s: float = 0.01):
+        self.samples, self.period, self.err = [], period_s, None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            import torch
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(torch_device).uuid)
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid) if not uuid.startswith("GPU-") else uuid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001 - report, do not fail the benchmark
+            self.err = f"{type(e).__name__}: {e}"
+
+    def _run(self):
+        p, h = self.nvml, self.handle
+        while not self._stop.is_set():
+            try:
+                sm = p.nvmlDeviceGetClockInfo(h, p.NVML_CLOCK_SM)
+                get = getattr(p, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    p.nvmlDeviceGetCurrentClocksThrottleReasons
+                reasons = get(h)
+                self.samples.append((sm, reasons))
+            except Exception as e:  # noqa: BLE001
+                self.err = str(e)
+                return
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.err is None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if self.err is not None and not self.samples:
+            return {"unavailable": self.err}
+        mask = 0
+        for _, r in self.samples:
+            mask |= r
+        reasons = sorted(name for bit, name in NVML_REASONS.items() if mask & bit)
+        return {"sm_mhz": statistics.median(s for s, _ in self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples),
+                "source": "NVML every 10 ms during the timed region"}
+
+
+# ----------------------------------------------------------------------------- CPU side (oracle)
+
+def make_host_step(shape, rows: int, seed: int = 0):
+    """Host buffers of `rows` tokens of `shape` for the CPU implementation (the
+    oracle's layer step). Values are tiled from a seeded N(0,1) block."""
+    import numpy as np
+
+    from oracle import oracle as orc
+
+    rng = np.random.default_rng(seed)
+    block = rng.standard_normal(1 << 22).astype(np.float32)
+    is_bf16 = shape.es == 2
+    if is_bf16:
+        block = orc.f32_to_bf16(block)
+    dt = np.uint16 if is_bf16 else np.float32
+
+    def fill(n, scale=1.0, offset=0.0):
+        src = block
+        if scale != 1.0 or offset != 0.0:
+            f = (orc.bf16_to_f32(block) if is_bf16 else block) * scale + offset
+            src = orc.f32_to_bf16(f) if is_bf16 else f.astype(np.float32)
+        out = np.empty(n, dt)
+        for i in range(0, n, src.size):
+            m = min(src.size, n - i)
+            out[i:i + m] = src[:m]
+        return out
+
+    R, D = rows, shape.dim
+    bufs = {
+        "ids": rng.integers(0, shape.vocab, R, dtype=np.int32),
+        "embed": fill(shape.vocab * D, 0.02),
+        "hidden": np.empty(R * D, dt),
+        "attn_out": fill(R * D),
+        "w_attn": fill(D, 0.02, 1.0),
+        "normed": np.empty(R * D, dt),
+        "q": fill(R * shape.hq * shape.hd),
+        "k": fill(R * shape.hkv * shape.hd),
+        "v": fill(R * shape.hkv * shape.hd),
+        "k_cache": np.zeros(shape.num_seqs * shape.hkv * shape.max_seq * shape.hd, dt),
+        "v_cache": np.zeros(shape.num_seqs * shape.hkv * shape.max_seq * shape.hd, dt),
+        "ffn_out": fill(R * D),
+        "w_ffn": fill(D, 0.02, 1.0),
+        "gate": fill(R * shape.ffn),
+        "up": fill(R * shape.ffn),
+        "act": np.empty(R * shape.ffn, dt),
+    }
+    if shape.positions == "uniform":
+        bufs["positions"] = rng.integers(0, shape.max_seq, R, dtype=np.int32)
+        bufs["seq_ids"] = (np.arange(R) % shape.num_seqs).astype(np.int32)
+    else:
+        r = np.arange(R, dtype=np.int64)
+        bufs["positions"] = (r % shape.max_seq).astype(np.int32)
+        bufs["seq_ids"] = ((r // shape.max_seq) % shape.num_seqs).astype(np.int32)
+    st = orc.OracleStep()
+    st.rows, st.dim, st.vocab, st.ffn = R, D, shape.vocab, shape.ffn
+    st.hq, st.hkv, st.hd, st.max_seq, st.num_seqs, st.table_len = (shape.hq, shape.hkv, shape.hd, shape.max_seq,
+                                                                   shape.num_seqs, 0)
+    st.eps, st.theta, st.dtype = shape.eps, shape.theta, 1 if is_bf16 else 0
+    for name, arr in bufs.items():
+        setattr(st, name, arr.ctypes.data)
+    return st, bufs
+
+
+def seconds_per_row(shape) -> float:
+    """One thread's time for one token of the CPU layer step (8-token probe; a small
+    vocabulary keeps the probe's embedding table small, the per-token work is the same)."""
+    import dataclasses
+
+    from oracle import oracle as orc
+
+    probe = dataclasses.replace(shape, vocab=min(shape.vocab, 1024))
+    calib = min(shape.rows, 8)
+    st, keep = make_host_step(probe, calib)
+    orc.layer_step(st, 0, calib, 1)
+    t0 = time.perf_counter()
+    orc.layer_step(st, 0, calib, 1)
+    del keep
+    return max((time.perf_counter() - t0) / calib, 1e-7)
+
+
+HOST_SAMPLE_BYTES = 8e9  # cap on the CPU sample's host buffers
+
+
+def sample_rows(shape, threads: int, seconds: float, per_row: float) -> int:
+    """Tokens the CPU sample covers: about `seconds` of work on `threads` threads,
+    at least one per thread, within the workload and the host-memory cap."""
+    by_mem = int(HOST_SAMPLE_BYTES // max(1, shape.with_rows(1).step_bytes()))
+    return int(max(1, min(shape.rows, by_mem, max(threads, seconds * threads / per_row))))
+
+
+def cpu_baseline(shape, threads: int, target_s: float, total_steps: int = 1):
+    """Times the oracle's layer step on a bounded row sample with `threads` host
+    threads. Returns (GB/s, rows sampled, seconds per step list)."""
+    from oracle import oracle as orc
+
+    rows = sample_rows(shape, threads, target_s / total_steps, seconds_per_row(shape))
+    st, keep = make_host_step(shape, rows)
+    orc.layer_step(st, 0, rows, threads)  # warm the pages
+    times = []
+    for _ in range(total_steps):
+        t0 = time.perf_counter()
+        bad = orc.layer_step(st, 0, rows, threads)
+        times.append(time.perf_counter() - t0)
+        assert bad == 0, bad
+    gbs = shape.with_rows(rows).step_bytes() / statistics.median(times) / 1e9
+    return gbs, rows, times
+
+
+def run_reference(args, shape):
+    """--impl reference: rank 0 times the CPU implementation; other ranks exit."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = host_threads()
+    K, W = args.steps, args.warmup
+    # each step is a bounded sample sized so the whole run takes about two minutes
+    per_step = max(0.5, 90.0 / max(1, K + W))
+    from oracle import oracle as orc
+
+    rows = sample_rows(shape, threads, per_step, seconds_per_row(shape))
+    st, keep = make_host_step(shape, rows)
+    for _ in range(W):
+        orc.layer_step(st, 0, rows, threads)
+    t0 = time.perf_counter()
+    for _ in range(K):
+        orc.layer_step(st, 0, rows, threads)
+    elapsed = time.perf_counter() - t0
+    sample_bytes = shape.with_rows(rows).step_bytes()
+    value = sample_bytes * K / elapsed / 1e9
+    sample = (f"{rows} of {shape.rows} tokens of one {shape.name} layer step per step (gather, add+RMSNorm, "
+              f"RoPE+KV store, add+RMSNorm, SwiGLU), oracle_layer_step_mt on {threads} threads")
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": K, "warmup": W,
+        "ms_per_step": round(elapsed / K * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16" if shape.es == 2 else "f32", "data": "synthetic (seeded N(0,1))",
+        "impl": "reference",
+        "config": config_dict(shape, args.gpus),
+        "rows_per_s": round(rows * K / elapsed, 1),
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_dict(shape, n):
+    return {"workload": shape.name, "description": shape.description, "rows_per_gpu": shape.rows,
+            "global_rows": shape.rows * n, "dim": shape.dim, "q_heads": shape.hq, "kv_heads": shape.hkv,
+            "head_dim": shape.hd, "ffn": shape.ffn, "vocab": shape.vocab, "rope_theta": shape.theta,
+            "max_seq": shape.max_seq, "sequences_per_gpu": shape.num_seqs,
+            "l2": f"inputs larger than L2: {shape.step_bytes() / 1e9:.2f} GB moved per step vs 126 MB L2"
+                  if shape.step_bytes() > 4 * 126e6 else "L2 not flushed: working set is L2-resident",
+            "parallelism": f"rows{n}: tokens partitioned across {n} GPU(s), no collectives"}
+
+
+# ----------------------------------------------------------------------------- main (ours)
+
+def main() -> int:
+    args = parse_args()
+    from baremetalinferenceengine_b200.layer import WORKLOADS
+
+    shape = WORKLOADS[args.workload]
+    if args.rows:
+        shape = shape.with_rows(args.rows)
+    if args.impl == "reference":
+        return run_reference(args, shape)
+
+    import torch
+    import torch.distributed as dist
+
+    from baremetalinferenceengine_b200 import layer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        log(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 under torchrun")
+        return 2
+    assert torch.cuda.is_available(), "bench.py needs CUDA devices"
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(values):
+        t = torch.tensor(values, dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
+
+    K, W = args.steps, args.warmup
+    if W < 3:
+        log("warning: fewer than 3 warm-up steps")
+    log(f"[rank {rank}] allocating {shape.name}: {shape.rows} tokens, {shape.step_bytes() / 1e9:.2f} GB per step")
+    b = layer.LayerBuffers(shape, dev, seed=1000 + rank, row_offset=rank * shape.rows)
+    stream = torch.cuda.Stream(dev)
+    kernels = shape.step_kernels()
+    nk = len(kernels)
+
+    with torch.cuda.stream(stream):
+        for _ in range(W):
+            layer.run_step(b, stream)
+    stream.synchronize()
+    assert b.status.read(stream) == 0, "device status set during warm-up"
+
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)] for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(dev) as clocks:
+        start.record(stream)
+        for i in range(K):
+            launches += layer.run_step(b, stream, events[i])
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    elapsed_ms = start.elapsed_time(end)
+    per_kernel = [statistics.mean(events[i][j].elapsed_time(events[i][j + 1]) for i in range(K)) for j in range(nk)]
+    assert b.status.read(stream) == 0, "device status set during the timed steps"
+    res = max_over_ranks([elapsed_ms] + per_kernel)
+    elapsed_ms, per_kernel = res[0], res[1:]
+
+    peak, peak_kind = measured_peak()
+    step_bytes = shape.step_bytes()
+    value = world * step_bytes * K / (elapsed_ms / 1e3) / 1e9
+    kern = {}
+    for (name, nbytes), ms in zip(kernels, per_kernel):
+        gbs = nbytes / (ms / 1e3) / 1e9
+        kern[name] = {"ms": round(ms, 4), "gb_per_launch": round(nbytes / 1e9, 4), "gbs": round(gbs, 1),
+                      "frac": round(gbs / peak, 4)}
+    dom_name, dom_bytes = max(kernels, key=lambda kv: kv[1])
+    dom_ms = per_kernel[[k for k, _ in kernels].index(dom_name)]
+    traffic = load_traffic(shape.name, dom_name)
+    roofline = {"kernel": dom_name, "bound": "hbm", "achieved": round(dom_bytes / (dom_ms / 1e3) / 1e9, 1),
+                "peak": peak, "unit": "GB/s", "frac": round(dom_bytes / (dom_ms / 1e3) / 1e9 / peak, 4),
+                "traffic": traffic, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                if peak_kind == "measured" else "fallback 6650 GB/s",
+                "algorithmic_bytes_per_launch": dom_bytes}
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(elapsed_ms / K, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16" if shape.es == 2 else "f32",
+        "data": "synthetic: seeded N(0,1) activations, 1+N(0,0.02) norm weights, N(0,0.02) embeddings",
+        "impl": "ours", "config": config_dict(shape, world),
+        "rows_per_s": round(world * shape.rows * K / (elapsed_ms / 1e3), 1),
+        "frac_of_peak": round(value / world / peak, 4),
+        "kernels": kern, "roofline": roofline, "gpu_launches": launches,
+        "clocks": clocks.summary() if rank == 0 else None,
+    }
+
+    # ---- end to end: inputs from pinned host memory, outputs back, every step
+    if not args.no_e2e:
+        line["e2e"] = e2e(args, b, shape, dev, world, barrier, max_over_ranks)
+    # ---- CPU baseline (rank 0, one GPU only)
+    if world == 1 and not args.no_cpu_baseline:
+        threads = host_threads()
+        gbs, rows, times = cpu_baseline(shape, threads, args.cpu_seconds)
+        line["cpu_baseline"] = {
+            "value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} of {shape.rows} tokens of one step (all five ops), oracle_layer_step_mt, "
+                      f"{times[0]:.1f} s on {threads} threads"}
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def load_traffic(workload: str, kernel: str):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if any."""
+    path = os.path.join(REPO, "profiles", "dram_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)[workload][kernel]["dram_bytes_per_launch"]
+    except (OSError, KeyError, ValueError, TypeError):
+        return None
+
+
+def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
+    """The same step through the public API with host buffers: every step copies
+    its inputs in from pinned host memory and its outputs back, chunked over rows
+    so copies in both directions overlap the kernels of other chunks."""
+    import torch
+
+    from baremetalinferenceengine_b200 import layer
+
+    names_in, names_out = layer.LayerBuffers.INPUTS, layer.LayerBuffers.OUTPUTS
+    def pinned(t):
+        return torch.empty(t.shape, dtype=t.dtype, device="cpu", pin_memory=True)
+
+    h_in = {n: pinned(getattr(b, n)) for n in names_in}
+    h_out = {n: pinned(getattr(b, n)) for n in names_out}
+    for n in names_in:
+        h_in[n].copy_(getattr(b, n))
+    h2d, comp, d2h = (torch.cuda.Stream(dev) for _ in range(3))
+    R = shape.rows
+    chunks = max(1, min(args.e2e_chunks, R))
+    size = math.ceil(R / chunks)
+    slices = [slice(i, min(R, i + size)) for i in range(0, R, size)]
+    done = torch.cuda.Event()
+
+    def step():
+        h2d.wait_event(done)
+        comp.wait_event(done)
+        for sl in slices:
+            ev_in, ev_k = torch.cuda.Event(), torch.cuda.Event()
+            with torch.cuda.stream(h2d):
+                for n in names_in:
+                    getattr(b, n)[sl].copy_(h_in[n][sl], non_blocking=True)
+                ev_in.record(h2d)
+            comp.wait_event(ev_in)
+            with torch.cuda.stream(comp):
+                layer.run_step(b, comp, rows=sl)
+                ev_k.record(comp)
+            d2h.wait_event(ev_k)
+            with torch.cuda.stream(d2h):
+                for n in names_out:
+                    h_out[n][sl].copy_(getattr(b, n)[sl], non_blocking=True)
+        done.record(d2h)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize(dev)
+    E = max(1, args.e2e_steps)
+    barrier()
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(h2d)
+    comp.wait_event(t0)
+    d2h.wait_event(t0)
+    for _ in range(E):
+        step()
+    t1.record(d2h)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms = max_over_ranks([t0.elapsed_time(t1)])[0]
+    gbs = world * shape.step_bytes() * E / (ms / 1e3) / 1e9
+    return {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": b.nbytes(names_in),
+            "d2h_bytes_per_step": b.nbytes(names_out), "steps": E, "ms_per_step": round(ms / E, 2),
+            "chunks": len(slices),
+            "how": "per step: pinned-host -> device copies of every input, the five kernels, device -> pinned-host "
+                   "copies of every output, chunked over rows on three streams; CUDA events, max over ranks"}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

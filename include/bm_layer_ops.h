@@ -1,0 +1,191 @@
+/*
+ * bm_layer_ops.h — C ABI of the B200 (sm_100a) fused transformer-layer kernels.
+ *
+ * The memory-bound per-token ops of a Llama layer, batched over rows (tokens):
+ * token-embedding gather, RMSNorm (optionally fused with the residual add),
+ * RoPE on Q and the GQA K heads written into a static KV cache, and SwiGLU.
+ *
+ * Conventions shared by every entry point:
+ *   - Plain pointers and sizes only. Every data pointer is a device pointer on
+ *     the CUDA device that is current on the calling thread; `stream` is a
+ *     cudaStream_t of that device passed as void* (NULL = legacy default stream).
+ *   - Launches are asynchronous and stream-ordered; no entry point synchronises,
+ *     except bm_status_read, which says so.
+ *   - Nothing allocates device memory, except bm_rope_table_create.
+ *   - The return value is a bm_status_t. Host-side argument checks happen before
+ *     any launch: on failure nothing is launched. No entry point calls exit().
+ *   - Data types: BM_F32 (IEEE fp32) or BM_BF16 (bfloat16 storage, 2 bytes).
+ *     Arithmetic is fp32 in every kernel; outputs are rounded to nearest-even.
+ *   - Rows are dense and row-major unless a stride argument says otherwise.
+ *     16-byte aligned pointers with 16-byte multiple row pitches take the
+ *     128-bit vector path; anything else runs a scalar path with the same
+ *     results.
+ *   - Values that only the device can check (token ids, positions and sequence
+ *     ids held in device arrays) are checked by the kernels. A bad row is skipped
+ *     (its outputs are left unwritten) and a BM_DEVERR_* bit is OR-ed into
+ *     *d_status when d_status is not NULL. Read it with bm_status_read.
+ *
+ * Each entry point cites the reference interface it replaces
+ * (NolanKisser/BareMetalInferenceEngine, paths within that project).
+ */
+#ifndef BM_LAYER_OPS_H
+#define BM_LAYER_OPS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BM_ABI_VERSION 1
+
+typedef enum bm_dtype {
+  BM_F32 = 0,
+  BM_BF16 = 1
+} bm_dtype_t;
+
+typedef enum bm_status {
+  BM_OK = 0,
+  BM_ERR_INVALID_ARGUMENT = 1, /* a size, pointer or dtype fails a host-side check */
+  BM_ERR_CUDA = 2,             /* a CUDA runtime call or launch failed */
+  BM_ERR_DEVICE = 3            /* bm_status_read found BM_DEVERR_* bits set */
+} bm_status_t;
+
+/* Bits a kernel OR-s into *d_status. */
+#define BM_DEVERR_BAD_ID 0x1       /* token id outside [0, vocab) */
+#define BM_DEVERR_BAD_POSITION 0x2 /* position outside [0, max_seq) or beyond the RoPE table */
+#define BM_DEVERR_BAD_SEQUENCE 0x4 /* sequence id outside [0, num_seqs) */
+
+/* Human-readable name of a bm_status_t. Never NULL. */
+const char* bm_status_string(int status);
+
+/* BM_ABI_VERSION of the loaded library. */
+int bm_abi_version(void);
+
+/* Message of the last BM_ERR_* returned on this host thread ("" if none). */
+const char* bm_last_error_message(void);
+
+/* Synchronises `stream`, copies *d_status into *flags_out (host) and clears
+ * *d_status to 0. Returns BM_ERR_DEVICE when any bit was set, else BM_OK. */
+int bm_status_read(int32_t* d_status, int32_t* flags_out, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Embedding gather: out[r, :] = table[ids[r], :]  (bit-exact copy).
+ * Replaces the per-token row copy in ExecutionEngine::run_layers
+ * (src/execution_engine.cu:98-99) and the host id check of forward()
+ * (src/execution_engine.cu:63-65), which becomes BM_DEVERR_BAD_ID.
+ * table: [vocab][dim]; out: rows of `dim` elements, `out_row_stride` elements
+ * apart (>= dim).
+ */
+int bm_embed_gather(void* out, const void* table, const int32_t* ids,
+                    int64_t rows, int64_t dim, int64_t vocab,
+                    int64_t out_row_stride, bm_dtype_t dtype,
+                    int32_t* d_status, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * RMSNorm over rows: out[r,i] = in[r,i] * rsqrt(mean_i(in[r,:]^2) + eps) * weight[i].
+ * Replaces launch_rms_norm (include/kernels.cuh:9, src/kernels.cu:59-78), which
+ * normalises one vector per launch. out may equal in (in place).
+ * in/out rows are in_stride / out_stride elements apart (>= dim).
+ */
+int bm_rmsnorm(void* out, const void* in, const void* weight,
+               int64_t rows, int64_t dim, float eps,
+               int64_t in_stride, int64_t out_stride,
+               bm_dtype_t dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused residual add + RMSNorm:
+ *   residual[r,:] <- residual[r,:] + delta[r,:]      (fp32 add, stored in dtype)
+ *   out[r,:]       = rmsnorm(residual[r,:]) * weight (on the stored values)
+ * Replaces the pair launch_add(hidden, hidden, projected) followed by
+ * launch_rms_norm(normed, hidden, w) (src/execution_engine.cu:118+121 and
+ * :126+:109/:80; include/kernels.cuh:9,32). Rows are dense ([rows][dim]).
+ * out must not overlap residual or delta.
+ */
+int bm_add_rmsnorm(void* residual, const void* delta, const void* weight,
+                   void* out, int64_t rows, int64_t dim, float eps,
+                   bm_dtype_t dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Element-wise add: out = a + b over n elements. out may equal a or b.
+ * Replaces launch_add (include/kernels.cuh:32, src/kernels.cu:199-207).
+ */
+int bm_add(void* out, const void* a, const void* b, int64_t n,
+           bm_dtype_t dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * SwiGLU: out = silu(gate) * up = gate / (1 + exp(-gate)) * up over n elements.
+ * Replaces launch_swiglu (include/kernels.cuh:29, src/kernels.cu:185-195).
+ * out may equal gate or up.
+ */
+int bm_swiglu(void* out, const void* gate, const void* up, int64_t n,
+              bm_dtype_t dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * RoPE table: fp32 (cos, sin) pairs laid out [max_pos][head_dim/2], entry
+ * (p, i) for angle p / theta^(2i/head_dim), computed on the device in fp64
+ * (the angle formula of the reference's CPU check loop,
+ * tests/kernel_tests.cu:180, rounded once to fp32).
+ * bm_rope_table_fill writes caller memory of max_pos*head_dim*4 bytes;
+ * bm_rope_table_create allocates it (cudaMalloc) and fills it, synchronously.
+ */
+int bm_rope_table_fill(void* table, int32_t max_pos, int32_t head_dim,
+                       double theta, void* stream);
+int bm_rope_table_create(int32_t max_pos, int32_t head_dim, double theta,
+                         void** table_out);
+int bm_rope_table_destroy(void* table);
+
+/* ---------------------------------------------------------------------------
+ * Fused RoPE + KV-cache store for `rows` tokens.
+ *   q [rows][num_q_heads][head_dim]  rotated in place;
+ *   k [rows][num_kv_heads][head_dim] rotated and written to k_cache (k itself
+ *                                    is not modified);
+ *   v [rows][num_kv_heads][head_dim] copied to v_cache.
+ * Caches are [num_seqs][num_kv_heads][max_seq][head_dim] (include/kv_cache.h:37-40).
+ * Token r goes to sequence seq_ids[r] (all 0 when seq_ids is NULL) at position
+ * positions[r] (pos0 + r when positions is NULL).
+ * Rotation: the half-split pairing (i, i + head_dim/2) of launch_rope
+ * (include/kernels.cuh:12-15, src/kernels.cu:126-140). Replaces the sequence
+ * launch_rope + launch_kv_store(k) + launch_kv_store(v)
+ * (src/execution_engine.cu:113-115; include/kernels.cuh:15,36).
+ * rope_table from bm_rope_table_*, with table_len positions; NULL computes
+ * cos/sin per pair on the device in fp64 from theta.
+ */
+int bm_rope_kv_store(void* q, const void* k, const void* v,
+                     const int32_t* positions, int32_t pos0,
+                     const int32_t* seq_ids,
+                     void* k_cache, void* v_cache,
+                     const void* rope_table, int32_t table_len, double theta,
+                     int64_t rows, int32_t num_q_heads, int32_t num_kv_heads,
+                     int32_t head_dim, int32_t max_seq, int32_t num_seqs,
+                     bm_dtype_t dtype, int32_t* d_status, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * RoPE in place on q [rows][num_q_heads][head_dim] and k [rows][num_kv_heads]
+ * [head_dim] (either may be NULL with its head count 0). Batched launch_rope
+ * (include/kernels.cuh:15, src/kernels.cu:126-148); positions/pos0,
+ * rope_table/theta as in bm_rope_kv_store.
+ */
+int bm_rope(void* q, void* k, const int32_t* positions, int32_t pos0,
+            const void* rope_table, int32_t table_len, double theta,
+            int64_t rows, int32_t num_q_heads, int32_t num_kv_heads,
+            int32_t head_dim, bm_dtype_t dtype, int32_t* d_status,
+            void* stream);
+
+/* ---------------------------------------------------------------------------
+ * KV store: cache[seq][h][pos][:] = src[r][h][:] for `rows` tokens.
+ * Batched launch_kv_store (include/kernels.cuh:36, src/kernels.cu:211-222);
+ * positions/pos0 and seq_ids as in bm_rope_kv_store.
+ */
+int bm_kv_store(void* cache, const void* src, const int32_t* positions,
+                int32_t pos0, const int32_t* seq_ids, int64_t rows,
+                int32_t num_heads, int32_t head_dim, int32_t max_seq,
+                int32_t num_seqs, bm_dtype_t dtype, int32_t* d_status,
+                void* stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* BM_LAYER_OPS_H */
