@@ -443,6 +443,18 @@ def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
     from baremetalinferenceengine_b200 import layer
 
     names_in, names_out = layer.LayerBuffers.INPUTS, layer.LayerBuffers.OUTPUTS
+    need = b.nbytes(names_in) + b.nbytes(names_out)
+    try:
+        import psutil
+
+        avail = psutil.virtual_memory().available
+    except ImportError:
+        avail = 0
+    # every rank pins its own copy; keep the total under 40% of what the host has free
+    if need * world > 0.4 * avail:
+        return {"unavailable": f"pinned host buffers of {need * world / 1e9:.1f} GB exceed 40% of the host's "
+                               f"{avail / 1e9:.1f} GB available memory"}
+
     def pinned(t):
         return torch.empty(t.shape, dtype=t.dtype, device="cpu", pin_memory=True)
 
