@@ -10,10 +10,12 @@
 // scalar loop with the same arithmetic.
 //
 // silu for fp32 I/O is g / (1 + expf(-g)) exactly as the reference writes it.
-// For bf16 I/O the reciprocal form g * rcp(1 + __expf(-g)) is used; its error
-// (a few fp32 ulp) is far below bf16 rounding. Both forms saturate the way the
-// reference's known-answer test expects (tests/kernel_tests.cu:164-173):
-// g = -1000 gives exp(1000) = inf and g / inf = -0; g = +1000 gives g * 1.
+// For bf16 I/O it is g * rcp(1 + 2^(-g log2 e)) on the special-function unit
+// (two MUFU instructions per element instead of a correctly rounded exp and
+// divide); its error (about 2^-21 relative) is far below bf16 rounding. Both
+// forms saturate the way the reference's known-answer test expects
+// (tests/kernel_tests.cu:164-173): g = -1000 gives exp(1000) = inf and
+// g / inf = -0; g = +1000 gives g * 1.
 #include <algorithm>
 
 #include "bm_common.cuh"
@@ -22,10 +24,27 @@
 namespace bm {
 namespace {
 
+#ifndef BM_EW_UNROLL
+#define BM_EW_UNROLL 4  // 16-byte vectors per operand a thread keeps in flight
+#endif
+#ifndef BM_EW_MINB
+#define BM_EW_MINB 1  // resident 256-thread blocks per SM the register budget must allow
+#endif
 constexpr int kThreads = 256;
-constexpr int kUnroll = 4;
+constexpr int kUnroll = BM_EW_UNROLL;
 
 enum class Op { kAdd, kSwiglu };
+
+// exp(-g) = 2^(-g * log2(e)) with the hardware's ex2.approx, and the reciprocal
+// with rcp.approx (both single MUFU instructions; relative errors near 2^-22).
+// ex2 of a large argument is +inf and rcp(+inf) is +0, so silu(-1000) = -0 and
+// silu(+1000) = 1000 exactly as in the reference's known-answer test.
+__device__ __forceinline__ float silu_fast(float g) {
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(g * -1.4426950408889634f));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+  return g * r;
+}
 
 template <typename T, Op OP>
 __device__ __forceinline__ float apply(float a, float b) {
@@ -34,12 +53,12 @@ __device__ __forceinline__ float apply(float a, float b) {
   } else if constexpr (sizeof(T) == 4) {
     return a / (1.0f + expf(-a)) * b;
   } else {
-    return a * __frcp_rn(1.0f + __expf(-a)) * b;
+    return silu_fast(a) * b;
   }
 }
 
 template <typename T, Op OP>
-__global__ void __launch_bounds__(kThreads) binary_vec_kernel(T* out, const T* a, const T* b,
+__global__ void __launch_bounds__(kThreads, BM_EW_MINB) binary_vec_kernel(T* out, const T* a, const T* b,
                                                              int64_t n) {
   constexpr int N = VecWidth<T>::value;
   const int64_t nvec = n / N;

@@ -54,6 +54,7 @@ struct RopeArgs {
   int upv;                    // pair units per head (half / VEC)
   int cpv;                    // copy units per head (hd / VEC)
   int q_units, k_units, total_units;
+  bool table_vec4;            // table 16-byte aligned: (cos, sin) pairs read two at a time
   int32_t* status;
 };
 
@@ -75,6 +76,17 @@ struct Chunk<T, 1> {
   __device__ __forceinline__ void get(float* f) const { f[0] = x; }
   __device__ __forceinline__ void set(const float* f) { x = f[0]; }
 };
+
+// (cos, sin) of pos / theta^(2i/hd) in fp64, rounded once to fp32: the angle of
+// the reference's CPU check loop (tests/kernel_tests.cu:180). Kept out of line:
+// it is the cold path (no table), and inlined fp64 pow/sincos would swell the
+// hot loops' register counts.
+__device__ __noinline__ float2 angle_cos_sin(int pos, int i, double theta, int hd) {
+  const double angle = static_cast<double>(pos) / pow(theta, 2.0 * i / hd);
+  double s, c;
+  sincos(angle, &s, &c);
+  return make_float2(static_cast<float>(c), static_cast<float>(s));
+}
 
 // Where unit u of a token lives: kind 0 = Q pair, 1 = K pair, 2 = V copy;
 // head h and chunk c within the head.
@@ -191,10 +203,7 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(RopeArgs a) {
         if (a.table != nullptr) {
           t = __ldg(a.table + static_cast<int64_t>(pos) * a.half + i);
         } else {
-          const double angle = static_cast<double>(pos) / pow(a.theta, 2.0 * i / a.hd);
-          double s, c;
-          sincos(angle, &s, &c);
-          t = make_float2(static_cast<float>(c), static_cast<float>(s));
+          t = angle_cos_sin(pos, i, a.theta, a.hd);
         }
         cs[i] = t;
       }
@@ -219,6 +228,161 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(RopeArgs a) {
   }
 }
 
+// Warp-per-token variant for large batches. Lane l owns pair chunk c = l % upv
+// of every head, so the VEC (cos, sin) pairs of that chunk are fetched once per
+// token and stay in registers for all of the token's Q and K heads; lanes
+// l / upv = 0..hpi-1 take heads h0, h0 + hpi, ... (hpi = 32 / upv heads per
+// pass, UNROLL passes' loads in flight together). No shared memory and no block
+// barrier: tokens on different warps never wait on one another.
+#ifndef BM_ROPE_WARP_UNROLL
+#define BM_ROPE_WARP_UNROLL 2  // passes whose loads a lane keeps in flight
+#endif
+#ifndef BM_ROPE_WARP_MINB
+#define BM_ROPE_WARP_MINB 4  // resident 256-thread blocks per SM the register budget must allow
+#endif
+#ifndef BM_ROPE_WARP_MIN_ROWS
+#define BM_ROPE_WARP_MIN_ROWS 512  // smaller batches: one block per token spreads a token wider
+#endif
+constexpr int kWarpUnroll = BM_ROPE_WARP_UNROLL;
+constexpr int64_t kWarpKernelMinRows = BM_ROPE_WARP_MIN_ROWS;
+
+template <typename T, int VEC>
+__device__ __forceinline__ void rotate(Chunk<T, VEC>& c1, Chunk<T, VEC>& c2, const float2* cs) {
+  float x1[VEC], x2[VEC];
+  c1.get(x1);
+  c2.get(x2);
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) {
+    const float first = x1[e], second = x2[e];
+    x1[e] = first * cs[e].x - second * cs[e].y;
+    x2[e] = second * cs[e].x + first * cs[e].y;
+  }
+  c1.set(x1);
+  c2.set(x2);
+}
+
+template <typename T, int VEC, int MODE>
+__global__ void __launch_bounds__(256, BM_ROPE_WARP_MINB) rope_kv_warp_kernel(RopeArgs a) {
+  constexpr int U = kWarpUnroll;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int upv = MODE == kStore ? 1 : a.upv;  // host guarantees 1 <= upv <= 32 for pair modes
+  const int hpi = 32 / upv;
+  const int c = lane % upv;
+  const int h0 = lane / upv;
+  const bool pair_lane = MODE != kStore && h0 < hpi;
+  const int64_t cache_head_stride = static_cast<int64_t>(a.max_seq) * a.hd;
+  const int nv = a.hkv * a.cpv;
+
+  for (int64_t row = warp; row < a.rows; row += nwarps) {
+    const int32_t pos = a.positions ? a.positions[row] : static_cast<int32_t>(a.pos0 + row);
+    const int32_t seq = a.seq_ids ? a.seq_ids[row] : 0;
+    int32_t bad = 0;
+    if (pos < 0) bad |= BM_DEVERR_BAD_POSITION;
+    if (MODE != kRope) {
+      if (pos >= a.max_seq) bad |= BM_DEVERR_BAD_POSITION;
+      if (seq < 0 || seq >= a.num_seqs) bad |= BM_DEVERR_BAD_SEQUENCE;
+    }
+    if (MODE != kStore && a.table != nullptr && pos >= a.table_len) bad |= BM_DEVERR_BAD_POSITION;
+    if (bad) {  // uniform across the warp
+      if (lane == 0) raise_status(a.status, bad);
+      continue;
+    }
+    const int64_t cache_base =
+        MODE == kRope ? 0 : (static_cast<int64_t>(seq) * a.hkv * a.max_seq + pos) * a.hd;
+
+    if (pair_lane) {
+      float2 cs[VEC];
+      if (a.table != nullptr) {
+        const float2* t = a.table + static_cast<int64_t>(pos) * a.half + c * VEC;
+        if (VEC % 2 == 0 && a.table_vec4) {
+#pragma unroll
+          for (int e = 0; e + 1 < VEC; e += 2) {
+            const float4 two = __ldg(reinterpret_cast<const float4*>(t + e));
+            cs[e] = make_float2(two.x, two.y);
+            cs[e + 1] = make_float2(two.z, two.w);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) cs[e] = __ldg(t + e);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) cs[e] = angle_cos_sin(pos, c * VEC + e, a.theta, a.hd);
+      }
+      // Q: rotated in place
+      T* qrow = static_cast<T*>(a.q) + row * a.hq * a.hd + c * VEC;
+      for (int hb = h0; hb < a.hq; hb += hpi * U) {
+        Chunk<T, VEC> x1[U], x2[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int h = hb + u * hpi;
+          if (h < a.hq) {
+            x1[u].load(qrow + static_cast<int64_t>(h) * a.hd);
+            x2[u].load(qrow + static_cast<int64_t>(h) * a.hd + a.half);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int h = hb + u * hpi;
+          if (h < a.hq) {
+            rotate<T, VEC>(x1[u], x2[u], cs);
+            x1[u].store(qrow + static_cast<int64_t>(h) * a.hd);
+            x2[u].store(qrow + static_cast<int64_t>(h) * a.hd + a.half);
+          }
+        }
+      }
+      // K: rotated into the cache (fused) or in place (rope only)
+      T* krow = static_cast<T*>(a.k) + row * a.hkv * a.hd + c * VEC;
+      for (int hb = h0; hb < a.hkv; hb += hpi * U) {
+        Chunk<T, VEC> x1[U], x2[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int h = hb + u * hpi;
+          if (h < a.hkv) {
+            x1[u].load(krow + static_cast<int64_t>(h) * a.hd);
+            x2[u].load(krow + static_cast<int64_t>(h) * a.hd + a.half);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int h = hb + u * hpi;
+          if (h < a.hkv) {
+            rotate<T, VEC>(x1[u], x2[u], cs);
+            T* dst = MODE == kFused
+                         ? static_cast<T*>(a.k_cache) + cache_base + h * cache_head_stride + c * VEC
+                         : krow + static_cast<int64_t>(h) * a.hd;
+            x1[u].store(dst);
+            x2[u].store(dst + a.half);
+          }
+        }
+      }
+    }
+    // V (fused) or src (store): copied into the cache, VEC elements per lane per pass
+    if (MODE != kRope) {
+      const T* vrow = static_cast<const T*>(a.v) + row * a.hkv * a.hd;
+      T* vdst = static_cast<T*>(a.v_cache) + cache_base;
+      for (int i0 = lane; i0 < nv; i0 += 32 * U) {
+        Chunk<T, VEC> d[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = i0 + u * 32;
+          if (i < nv) d[u].load(vrow + static_cast<int64_t>(i) * VEC);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int i = i0 + u * 32;
+          if (i < nv) {
+            const int h = i / a.cpv;
+            d[u].store(vdst + h * cache_head_stride + (i - h * a.cpv) * VEC);
+          }
+        }
+      }
+    }
+  }
+}
+
 __global__ void rope_table_kernel(float2* table, int32_t max_pos, int half, int hd, double theta) {
   const int64_t n = static_cast<int64_t>(max_pos) * half;
   for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < n;
@@ -234,6 +398,12 @@ __global__ void rope_table_kernel(float2* table, int32_t max_pos, int half, int 
 
 template <typename T, int VEC, int MODE>
 int launch_typed(const RopeArgs& a, cudaStream_t stream, const char* what) {
+  if (a.rows >= kWarpKernelMinRows && (MODE == kStore || (a.upv >= 1 && a.upv <= 32))) {
+    const int64_t blocks = (a.rows + 7) / 8;  // 8 warps (tokens in flight) per 256-thread block
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(blocks, static_cast<int64_t>(sm_count()) * 16));
+    rope_kv_warp_kernel<T, VEC, MODE><<<grid, 256, 0, stream>>>(a);
+    return check_launch(what);
+  }
   const int want = (a.total_units + kUPT - 1) / kUPT;
   const int block = std::min(256, std::max(64, (want + 31) / 32 * 32));
   const int64_t cap = static_cast<int64_t>(sm_count()) * (2048 / block);
@@ -253,6 +423,7 @@ int launch(RopeArgs a, bm_dtype_t dtype, cudaStream_t stream, const char* what) 
     if (p != nullptr && !aligned16(p)) vec_ok = false;
   }
   const int v_used = vec_ok ? vec : 1;
+  a.table_vec4 = a.table != nullptr && aligned16(a.table);
   a.upv = a.half / v_used;
   a.cpv = a.hd / v_used;
   if (MODE == kStore) {

@@ -319,6 +319,39 @@ def test_rope_kv_store(cuda, case, use_table):
     assert bits_equal(kd, k) and bits_equal(vd, v)  # k and v inputs are not modified
 
 
+@pytest.mark.parametrize("use_table", [True, False], ids=["table", "fp64"])
+@pytest.mark.parametrize("dt", DTYPES, ids=["f32", "bf16"])
+@pytest.mark.parametrize("rows,hq,hkv,hd", [(512, 6, 6, 48), (1024, 32, 8, 128), (600, 64, 8, 128), (700, 5, 1, 6),
+                                            (513, 4, 2, 34), (512, 2, 1, 1024)])
+def test_rope_kv_store_large_batches(cuda, use_table, dt, rows, hq, hkv, hd):
+    """Batches of >= 512 tokens take the warp-per-token kernel (heads spread over the
+    lanes, cos/sin kept in registers); head_dim 1024 falls back to one block per token."""
+    max_seq, num_seqs = 2048, 3
+    g = gen(rows + hq + hd)
+    q, k, v = randn((rows, hq, hd), dt, g), randn((rows, hkv, hd), dt, g), randn((rows, hkv, hd), dt, g)
+    perm = torch.randperm(num_seqs * max_seq, generator=g)[:rows]
+    pos, seq = (perm % max_seq).to(torch.int32), (perm // max_seq).to(torch.int32)
+    kc = torch.full((num_seqs, hkv, max_seq, hd), -3.0, dtype=dt)
+    vc = torch.full((num_seqs, hkv, max_seq, hd), 5.0, dtype=dt)
+    qd, kcd, vcd = q.to(cuda), kc.to(cuda), vc.to(cuda)
+    table = ops.RopeTable(max_seq, hd, 5e5, cuda) if use_table else None
+    ops.rope_kv_store(qd, k.to(cuda), v.to(cuda), pos.to(cuda), kcd, vcd, table=table, theta=5e5,
+                      seq_ids=seq.to(cuda))
+    want_q, want_kc, want_vc, _ = orc.rope_kv_store(to_np(q), to_np(k), to_np(v), pos.numpy(), to_np(kc), to_np(vc),
+                                                    5e5, seq_ids=seq.numpy())
+    assert worst(qd, want_q) <= TOL[dt]
+    assert worst(kcd, want_kc) <= TOL[dt]
+    assert bits_equal(vcd, from_np(want_vc))
+    # the in-place variant and the plain store at the same sizes
+    qd2, kd2 = q.to(cuda), k.to(cuda)
+    ops.rope(qd2, kd2, pos.to(cuda), table=table, theta=5e5)
+    assert worst(qd2, orc.rope(to_np(q), pos.numpy(), 5e5)) <= TOL[dt]
+    assert worst(kd2, orc.rope(to_np(k), pos.numpy(), 5e5)) <= TOL[dt]
+    vcd2 = vc.to(cuda)
+    ops.kv_store(vcd2, v.to(cuda), pos.to(cuda), seq.to(cuda))
+    assert bits_equal(vcd2, from_np(want_vc))
+
+
 @pytest.mark.parametrize("dt", DTYPES, ids=["f32", "bf16"])
 @pytest.mark.parametrize("hq,hkv,hd", [(6, 6, 48), (6, 3, 48), (8, 8, 128), (5, 1, 6), (4, 2, 34)])
 def test_rope_in_place(cuda, dt, hq, hkv, hd):
@@ -338,9 +371,12 @@ def test_rope_position_zero_is_identity(cuda):
     """tests/kernel_tests.cu:280: at position 0 the rotation is exactly the identity."""
     q = torch.randn(3, 6, 48)
     qd = q.to(cuda)
-    ops.rope(qd, None, 0, theta=1e4)
+    ops.rope(qd[:1], None, 0, theta=1e4)  # one token at pos0 = 0 (fp64 cos/sin)
     ops.rope(qd, None, torch.zeros(3, dtype=torch.int32, device=cuda), table=ops.RopeTable(8, 48, 1e4, cuda))
     assert bits_equal(qd, q)
+    ops.rope(qd, None, 0, theta=1e4)  # pos0 = 0 over 3 tokens means positions 0, 1, 2
+    want = orc.rope(q.numpy(), np.arange(3, dtype=np.int32), 1e4)
+    assert bits_equal(qd[0], q[0]) and worst(qd, want) <= 1e-5
 
 
 def test_rope_bad_positions_and_sequences_flag_and_skip(cuda):
