@@ -235,10 +235,10 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(RopeArgs a) {
 // pass, UNROLL passes' loads in flight together). No shared memory and no block
 // barrier: tokens on different warps never wait on one another.
 #ifndef BM_ROPE_WARP_UNROLL
-#define BM_ROPE_WARP_UNROLL 2  // passes whose loads a lane keeps in flight
+#define BM_ROPE_WARP_UNROLL 4  // passes whose loads a lane keeps in flight
 #endif
 #ifndef BM_ROPE_WARP_MINB
-#define BM_ROPE_WARP_MINB 4  // resident 256-thread blocks per SM the register budget must allow
+#define BM_ROPE_WARP_MINB 2  // resident 256-thread blocks per SM the register budget must allow
 #endif
 #ifndef BM_ROPE_WARP_MIN_ROWS
 #define BM_ROPE_WARP_MIN_ROWS 512  // smaller batches: one block per token spreads a token wider

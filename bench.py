@@ -238,16 +238,17 @@ def sample_rows(shape, threads: int, seconds: float, per_row: float) -> int:
     return int(max(1, min(shape.rows, by_mem, max(threads, seconds * threads / per_row))))
 
 
-def cpu_baseline(shape, threads: int, target_s: float, total_steps: int = 1):
+def cpu_baseline(shape, threads: int, target_s: float):
     """Times the oracle's layer step on a bounded row sample with `threads` host
-    threads. Returns (GB/s, rows sampled, seconds per step list)."""
+    threads, repeating the sample until about `target_s` of work is timed.
+    Returns (GB/s, rows sampled, seconds per repetition)."""
     from oracle import oracle as orc
 
-    rows = sample_rows(shape, threads, target_s / total_steps, seconds_per_row(shape))
+    rows = sample_rows(shape, threads, target_s, seconds_per_row(shape))
     st, keep = make_host_step(shape, rows)
     orc.layer_step(st, 0, rows, threads)  # warm the pages
     times = []
-    for _ in range(total_steps):
+    while not times or (sum(times) < target_s and len(times) < 50):
         t0 = time.perf_counter()
         bad = orc.layer_step(st, 0, rows, threads)
         times.append(time.perf_counter() - t0)
@@ -319,7 +320,7 @@ def main() -> int:
     import torch
     import torch.distributed as dist
 
-    from baremetalinferenceengine_b200 import layer
+    from baremetalinferenceengine_b200 import layer, shard
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -338,16 +339,14 @@ def main() -> int:
             dist.barrier()
 
     def max_over_ranks(values):
-        t = torch.tensor(values, dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return t.tolist()
+        return shard.max_over_ranks(values, device=dev)
 
     K, W = args.steps, args.warmup
     if W < 3:
         log("warning: fewer than 3 warm-up steps")
     log(f"[rank {rank}] allocating {shape.name}: {shape.rows} tokens, {shape.step_bytes() / 1e9:.2f} GB per step")
-    b = layer.LayerBuffers(shape, dev, seed=1000 + rank, row_offset=rank * shape.rows)
+    rows = shard.weak_rows(rank, world, shape.rows)  # this rank's tokens of the N x R job
+    b = layer.LayerBuffers(shape, dev, seed=1000 + rank, row_offset=rows.start)
     stream = torch.cuda.Stream(dev)
     kernels = shape.step_kernels()
     nk = len(kernels)
@@ -414,8 +413,8 @@ def main() -> int:
         gbs, rows, times = cpu_baseline(shape, threads, args.cpu_seconds)
         line["cpu_baseline"] = {
             "value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{rows} of {shape.rows} tokens of one step (all five ops), oracle_layer_step_mt, "
-                      f"{times[0]:.1f} s on {threads} threads"}
+            "sample": f"{rows} of {shape.rows} tokens of one step (all five ops), oracle_layer_step_mt on "
+                      f"{threads} threads, {len(times)} repetitions, {sum(times):.1f} s, median taken"}
 
     if world > 1:
         dist.destroy_process_group()
@@ -434,6 +433,44 @@ def load_traffic(workload: str, kernel: str):
         return None
 
 
+def pcie_link(dev, h2d, d2h, nbytes: int = 1 << 30, reps: int = 3) -> dict:
+    """Host<->device bandwidth of pinned copies (the roofline of the e2e leg):
+    H2D alone, D2H alone, and both directions at once on two streams."""
+    import torch
+
+    host_a = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    host_b = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    dev_a = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    dev_b = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+
+    def timed(streams_ops):
+        evs = []
+        for s, op in streams_ops:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(s):
+                e0.record(s)
+                for _ in range(reps):
+                    op()
+                e1.record(s)
+            evs.append((e0, e1))
+        torch.cuda.synchronize(dev)
+        return max(e0.elapsed_time(e1) for e0, e1 in evs) / 1e3
+
+    up = lambda: dev_a.copy_(host_a, non_blocking=True)  # noqa: E731
+    down = lambda: host_b.copy_(dev_b, non_blocking=True)  # noqa: E731
+    timed([(h2d, up), (d2h, down)])  # warm
+    t_up = timed([(h2d, up)])
+    t_down = timed([(d2h, down)])
+    t_both = timed([(h2d, up), (d2h, down)])
+    gb = nbytes * reps / 1e9
+    return {"h2d_gbs": round(gb / t_up, 1), "d2h_gbs": round(gb / t_down, 1),
+            "bidirectional_gbs": round(2 * gb / t_both, 1), "how": "pinned 1 GiB copies x3, CUDA events"}
+
+
+def bytes_per_row(b, names) -> float:
+    return b.nbytes(names) / b.shape.rows
+
+
 def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
     """The same step through the public API with host buffers: every step copies
     its inputs in from pinned host memory and its outputs back, chunked over rows
@@ -443,27 +480,29 @@ def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
     from baremetalinferenceengine_b200 import layer
 
     names_in, names_out = layer.LayerBuffers.INPUTS, layer.LayerBuffers.OUTPUTS
-    need = b.nbytes(names_in) + b.nbytes(names_out)
+    io_per_row = (b.nbytes(names_in) + b.nbytes(names_out)) / shape.rows
     try:
         import psutil
 
         avail = psutil.virtual_memory().available
     except ImportError:
         avail = 0
-    # every rank pins its own copy; keep the total under 40% of what the host has free
-    if need * world > 0.4 * avail:
-        return {"unavailable": f"pinned host buffers of {need * world / 1e9:.1f} GB exceed 40% of the host's "
-                               f"{avail / 1e9:.1f} GB available memory"}
+    # Every rank pins its own host buffers; all ranks together stay under 40% of
+    # the host's free memory. The step then covers the first R rows that fit
+    # (throughput in GB/s does not depend on R once R is thousands of tokens).
+    R = int(min(shape.rows, 0.4 * avail / world // io_per_row))
+    R = int(-max_over_ranks([-R])[0])  # the same rows (and the same branch) on every rank
+    if R < 1024:
+        return {"unavailable": f"host has {avail / 1e9:.1f} GB free: too little to pin a step's buffers"}
 
     def pinned(t):
-        return torch.empty(t.shape, dtype=t.dtype, device="cpu", pin_memory=True)
+        return torch.empty((R,) + tuple(t.shape[1:]), dtype=t.dtype, device="cpu", pin_memory=True)
 
     h_in = {n: pinned(getattr(b, n)) for n in names_in}
     h_out = {n: pinned(getattr(b, n)) for n in names_out}
     for n in names_in:
-        h_in[n].copy_(getattr(b, n))
+        h_in[n].copy_(getattr(b, n)[:R])
     h2d, comp, d2h = (torch.cuda.Stream(dev) for _ in range(3))
-    R = shape.rows
     chunks = max(1, min(args.e2e_chunks, R))
     size = math.ceil(R / chunks)
     slices = [slice(i, min(R, i + size)) for i in range(0, R, size)]
@@ -505,10 +544,14 @@ def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
     torch.cuda.synchronize(dev)
     barrier()
     ms = max_over_ranks([t0.elapsed_time(t1)])[0]
-    gbs = world * shape.step_bytes() * E / (ms / 1e3) / 1e9
-    return {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": b.nbytes(names_in),
-            "d2h_bytes_per_step": b.nbytes(names_out), "steps": E, "ms_per_step": round(ms / E, 2),
-            "chunks": len(slices),
+    link = pcie_link(dev, h2d, d2h)
+    gbs = world * shape.with_rows(R).step_bytes() * E / (ms / 1e3) / 1e9
+    h2d_rate = bytes_per_row(b, names_in) * R / (ms / E / 1e3) / 1e9
+    return {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": int(bytes_per_row(b, names_in) * R),
+            "d2h_bytes_per_step": int(bytes_per_row(b, names_out) * R), "rows_per_step": R, "steps": E,
+            "ms_per_step": round(ms / E, 2), "chunks": len(slices),
+            "link": link, "h2d_gbs_achieved": round(h2d_rate, 1),
+            "frac_of_link": round(h2d_rate / link["h2d_gbs"], 3) if link.get("h2d_gbs") else None,
             "how": "per step: pinned-host -> device copies of every input, the five kernels, device -> pinned-host "
                    "copies of every output, chunked over rows on three streams; CUDA events, max over ranks"}
 

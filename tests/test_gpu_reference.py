@@ -100,13 +100,14 @@ def test_legacy_symbols_single_token(cuda):
     assert orc.worst_error(kd.cpu().numpy(), orc.rope(k.numpy().reshape(1, hkv, hd), 4097, 5e5).ravel()) <= 1e-5
 
     gt, up = torch.randn(ffn, generator=g) * 3, torch.randn(ffn, generator=g)
+    gtd, upd = gt.cuda(), up.cuda()  # kept alive: a freed temporary's block could be reused by the next copy
     act = torch.empty(ffn, device=cuda)
-    f["launch_swiglu"](act.data_ptr(), gt.cuda().data_ptr(), up.cuda().data_ptr(), ffn, None)
+    f["launch_swiglu"](act.data_ptr(), gtd.data_ptr(), upd.data_ptr(), ffn, None)
     assert orc.worst_error(act.cpu().numpy(), orc.swiglu(gt.numpy(), up.numpy())) <= 1e-5
 
     a, b = torch.randn(dim, generator=g), torch.randn(dim, generator=g)
-    ad = a.cuda()
-    f["launch_add"](ad.data_ptr(), ad.data_ptr(), b.cuda().data_ptr(), dim, None)
+    ad, bd = a.cuda(), b.cuda()
+    f["launch_add"](ad.data_ptr(), ad.data_ptr(), bd.data_ptr(), dim, None)
     assert bits_equal(ad, a + b)
 
     cache = torch.randn(hkv, max_seq, hd, generator=g)
@@ -196,11 +197,36 @@ def test_ours_and_the_reference_kernels_against_the_oracle(cuda):
 
     # add (in place, as the engine's residual add)
     a, b = torch.randn(rows, dim, generator=g), torch.randn(rows, dim, generator=g)
-    ar, ao = a.cuda(), a.cuda()
-    R.ref_add(ar.data_ptr(), ar.data_ptr(), b.cuda().data_ptr(), rows * dim, None)
+    ar, ao, bd = a.cuda(), a.cuda(), b.cuda()
+    R.ref_add(ar.data_ptr(), ar.data_ptr(), bd.data_ptr(), rows * dim, None)
     ops.add(ao, b.cuda(), out=ao)
     assert bits_equal(ao, ar)
 
     print("worst error vs oracle (ours, reference kernels):", report)
     for name, (ours_err, ref_err) in report.items():
         assert ours_err <= 1e-5, (name, ours_err, ref_err)
+
+
+def test_reference_engine_runs_on_the_dropin(cuda, tmp_path):
+    """The reference's ExecutionEngine and its logits test (tests/logits_test.cu),
+    unmodified, built against this library for the five layer ops, reproduce the
+    logits of the same engine on the reference's own kernels: every position within
+    the test's 0.01 limit, the same next token everywhere, and the same logits after
+    a reset with the whole sequence in one call. The model is a seeded synthetic
+    export (no checkpoint is available); golden logits come from
+    oracle/_ref/engine_golden_ref (the reference's engine and kernels)."""
+    from tests.engine_export import write_export
+
+    for exe in ("engine_golden_ref", "logits_test_dropin"):
+        if not os.path.exists(os.path.join(orc.REF_DIR, exe)):
+            pytest.fail(f"oracle/_ref/{exe} is missing (make -C oracle ref)")
+    cfg = write_export(str(tmp_path), seed=11)
+    tokens = [int(t) for t in np.random.default_rng(12).integers(0, cfg["vocab"], 40)]
+    gold = subprocess.run([os.path.join(orc.REF_DIR, "engine_golden_ref"), str(tmp_path)] + [str(t) for t in tokens],
+                          capture_output=True, text=True, timeout=600)
+    assert gold.returncode == 0, gold.stdout[-2000:] + gold.stderr[-2000:]
+    run = subprocess.run([os.path.join(orc.REF_DIR, "logits_test_dropin"), str(tmp_path)], capture_output=True,
+                         text=True, timeout=600)
+    print(run.stdout[-1500:])
+    assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-2000:]
+    assert "0 check(s) failed" in run.stdout
