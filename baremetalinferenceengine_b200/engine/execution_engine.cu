@@ -1,0 +1,150 @@
+// execution_engine.cu — ExecutionEngine on the fused B200 layer ops (see the header).
+#include "execution_engine.h"
+
+#include <iostream>
+#include <stdexcept>
+
+#include "bm_layer_ops.h"
+#include "kernels.cuh"
+
+namespace {
+
+void check(int status, const char* what) {
+  if (status != BM_OK) {
+    throw std::runtime_error(std::string(what) + ": " + bm_status_string(status) + ": " + bm_last_error_message());
+  }
+}
+
+}  // namespace
+
+ExecutionEngine::ExecutionEngine(std::shared_ptr<MemoryAllocator> allocator, std::shared_ptr<KVCache> kv_cache,
+                                 const ModelConfig& config)
+    : allocator_(allocator), kv_cache_(kv_cache), config_(config) {
+  token_embeddings_ = weight("model.embed_tokens.weight");
+  final_norm_ = weight("model.norm.weight");
+  lm_head_ = weight("lm_head.weight");
+  for (int l = 0; l < config_.num_layers; ++l) {
+    const std::string p = "model.layers." + std::to_string(l) + ".";
+    layers_.push_back({weight(p + "input_layernorm.weight"), weight(p + "self_attn.q_proj.weight"),
+                       weight(p + "self_attn.k_proj.weight"), weight(p + "self_attn.v_proj.weight"),
+                       weight(p + "self_attn.o_proj.weight"), weight(p + "post_attention_layernorm.weight"),
+                       weight(p + "mlp.gate_proj.weight"), weight(p + "mlp.up_proj.weight"),
+                       weight(p + "mlp.down_proj.weight")});
+  }
+  const int max_seq = kv_cache_->get_max_seq_len();
+  scores_ = std::make_shared<DeviceBuffer<float>>(static_cast<size_t>(config_.num_heads) * max_seq);
+  logits_ = std::make_shared<DeviceBuffer<float>>(config_.vocab_size);
+  // (cos, sin) per position, computed once on the device in fp64 and kept in L2-sized fp32
+  rope_table_ = std::make_shared<DeviceBuffer<float>>(static_cast<size_t>(max_seq) * config_.head_dim());
+  check(bm_rope_table_fill(rope_table_->get(), max_seq, config_.head_dim(), config_.rope_theta, nullptr),
+        "bm_rope_table_fill");
+  reserve(1);
+}
+
+ExecutionEngine::~ExecutionEngine() {}
+
+float* ExecutionEngine::weight(const std::string& name) const {
+  float* tensor = static_cast<float*>(allocator_->get_device_tensor(name));
+  if (!tensor) throw std::runtime_error("Model is missing tensor " + name);
+  return tensor;
+}
+
+void ExecutionEngine::reserve(int tokens) {
+  if (tokens <= capacity_) return;
+  const size_t dim = config_.dim;
+  const size_t hidden = config_.hidden_dim;
+  const size_t n = static_cast<size_t>(tokens);
+  activations_.clear();
+  auto buffer = [&](size_t elements) {
+    activations_.push_back(std::make_shared<DeviceBuffer<float>>(elements));
+    return activations_.back()->get();
+  };
+  hidden_ = buffer(n * dim);
+  normed_ = buffer(n * dim);
+  q_ = buffer(n * dim);
+  k_ = buffer(n * dim);
+  v_ = buffer(n * dim);
+  attention_out_ = buffer(n * dim);
+  projected_ = buffer(n * dim);
+  gate_ = buffer(n * hidden);
+  up_ = buffer(n * hidden);
+  activated_ = buffer(n * hidden);
+  ids_ = std::make_shared<DeviceBuffer<int>>(n);
+  capacity_ = tokens;
+}
+
+void ExecutionEngine::reset() { kv_cache_->reset(); }
+
+std::vector<float> ExecutionEngine::forward(const std::vector<int>& input_tokens) {
+  // Argument checks and messages as the reference's forward (src/execution_engine.cu:62-69).
+  if (input_tokens.empty()) throw std::invalid_argument("forward() needs at least one token");
+  for (int token : input_tokens) {
+    if (token < 0 || token >= config_.vocab_size) {
+      throw std::invalid_argument("Token " + std::to_string(token) + " is outside the vocabulary");
+    }
+  }
+  const int max_seq = kv_cache_->get_max_seq_len();
+  const size_t end_pos = static_cast<size_t>(kv_cache_->get_current_seq_pos()) + input_tokens.size();
+  if (end_pos > static_cast<size_t>(max_seq)) {
+    throw std::runtime_error("Sequence would exceed the KV cache's " + std::to_string(max_seq) + " positions");
+  }
+  if (verbose_) std::cout << "Forward pass for " << input_tokens.size() << " tokens" << std::endl;
+
+  const int T = static_cast<int>(input_tokens.size());
+  reserve(T);
+  const int dim = config_.dim;
+  const int hidden_dim = config_.hidden_dim;
+  const int heads = config_.num_heads;
+  const int head_dim = config_.head_dim();
+  const int pos0 = kv_cache_->get_current_seq_pos();
+  const float eps = config_.norm_eps;
+
+  CUDA_CHECK(cudaMemcpy(ids_->get(), input_tokens.data(), sizeof(int) * T, cudaMemcpyHostToDevice));
+  check(bm_embed_gather(hidden_, token_embeddings_, ids_->get(), T, dim, config_.vocab_size, dim, BM_F32, nullptr,
+                        nullptr),
+        "bm_embed_gather");
+
+  for (int l = 0; l < config_.num_layers; ++l) {
+    const LayerWeights& w = layers_[l];
+    float* k_cache = kv_cache_->get_key_cache(l);
+    float* v_cache = kv_cache_->get_value_cache(l);
+
+    // The previous layer's residual add (its down projection) is fused into this norm.
+    if (l == 0) {
+      check(bm_rmsnorm(normed_, hidden_, w.attention_norm, T, dim, eps, dim, dim, BM_F32, nullptr), "bm_rmsnorm");
+    } else {
+      check(bm_add_rmsnorm(hidden_, projected_, w.attention_norm, normed_, T, dim, eps, BM_F32, nullptr),
+            "bm_add_rmsnorm");
+    }
+    launch_gemm(q_, normed_, w.q_proj, T, dim, dim);
+    launch_gemm(k_, normed_, w.k_proj, T, dim, dim);
+    launch_gemm(v_, normed_, w.v_proj, T, dim, dim);
+    // Positions pos0..pos0+T-1 of the one sequence the reference's cache holds.
+    check(bm_rope_kv_store(q_, k_, v_, nullptr, pos0, nullptr, k_cache, v_cache, rope_table_->get(), max_seq,
+                           config_.rope_theta, T, heads, heads, head_dim, max_seq, 1, BM_F32, nullptr, nullptr),
+          "bm_rope_kv_store");
+    // Token t attends to the cache positions up to its own.
+    for (int t = 0; t < T; ++t) {
+      launch_attention(attention_out_ + static_cast<size_t>(t) * dim, q_ + static_cast<size_t>(t) * dim, k_cache,
+                       v_cache, scores_->get(), heads, head_dim, max_seq, pos0 + t + 1);
+    }
+    launch_gemm(projected_, attention_out_, w.o_proj, T, dim, dim);
+    check(bm_add_rmsnorm(hidden_, projected_, w.ffn_norm, normed_, T, dim, eps, BM_F32, nullptr), "bm_add_rmsnorm");
+    launch_gemm(gate_, normed_, w.gate_proj, T, hidden_dim, dim);
+    launch_gemm(up_, normed_, w.up_proj, T, hidden_dim, dim);
+    check(bm_swiglu(activated_, gate_, up_, static_cast<int64_t>(T) * hidden_dim, BM_F32, nullptr), "bm_swiglu");
+    launch_gemm(projected_, activated_, w.down_proj, T, dim, hidden_dim);
+  }
+
+  // Only the last token's logits are returned: its final residual add and norm.
+  const size_t last = static_cast<size_t>(T - 1) * dim;
+  check(bm_add_rmsnorm(hidden_ + last, projected_ + last, final_norm_, normed_ + last, 1, dim, eps, BM_F32,
+                       nullptr),
+        "bm_add_rmsnorm");
+  launch_gemm(logits_->get(), normed_ + last, lm_head_, 1, config_.vocab_size, dim);
+  kv_cache_->increment_seq_pos(T);
+
+  std::vector<float> logits(config_.vocab_size);
+  CUDA_CHECK(cudaMemcpy(logits.data(), logits_->get(), logits.size() * sizeof(float), cudaMemcpyDeviceToHost));
+  return logits;
+}

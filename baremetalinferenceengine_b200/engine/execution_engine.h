@@ -1,0 +1,94 @@
+// execution_engine.h — drop-in ExecutionEngine on the batched, fused layer ops.
+//
+// The public interface is the reference's (include/execution_engine.h:11-74:
+// constructor, forward, reset, set_verbose, and the same exceptions), so the
+// reference's src/main.cpp, src/benchmark.cpp, src/server.cpp and
+// tests/logits_test.cu compile unchanged against this header. The
+// implementation (execution_engine.cu beside it) differs from the reference's
+// run_layers (src/execution_engine.cu:89-128) in two ways:
+//   - all tokens of one forward() call go through each layer together: one
+//     launch per op for the whole batch instead of one per token (attention,
+//     which needs each token's own causal length, still runs per token);
+//   - the memory-bound ops are the fused B200 kernels of bm_layer_ops.h: the
+//     embedding gather, the residual add fused into the RMSNorm that follows it
+//     (:118+:121, :126+:109, :126+:80), and RoPE fused with both KV-cache writes
+//     (:113-115).
+// The GEMM and attention kernels stay the reference's (launch_gemm,
+// launch_attention from its src/kernels.cu): they are outside the layer-op path.
+#ifndef EXECUTION_ENGINE_H
+#define EXECUTION_ENGINE_H
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "kv_cache.h"
+#include "memory_allocator.h"
+#include "weights.h"
+
+class ExecutionEngine {
+ public:
+  // Throws std::runtime_error if the allocator is missing a tensor the model needs.
+  ExecutionEngine(std::shared_ptr<MemoryAllocator> allocator, std::shared_ptr<KVCache> kv_cache,
+                  const ModelConfig& config);
+  ~ExecutionEngine();
+
+  // Feeds tokens through the model, extending the sequence held in the KV cache,
+  // and returns the logits that follow the last token. Throws
+  // std::invalid_argument for bad tokens, or std::runtime_error when the sequence
+  // would exceed the KV cache.
+  std::vector<float> forward(const std::vector<int>& input_tokens);
+
+  // Starts a new sequence.
+  void reset();
+
+  void set_verbose(bool verbose) { verbose_ = verbose; }
+
+ private:
+  struct LayerWeights {
+    float* attention_norm;
+    float* q_proj;
+    float* k_proj;
+    float* v_proj;
+    float* o_proj;
+    float* ffn_norm;
+    float* gate_proj;
+    float* up_proj;
+    float* down_proj;
+  };
+
+  float* weight(const std::string& name) const;
+  void reserve(int tokens);  // grows the per-token activation buffers
+
+  std::shared_ptr<MemoryAllocator> allocator_;
+  std::shared_ptr<KVCache> kv_cache_;
+  ModelConfig config_;
+
+  float* token_embeddings_ = nullptr;
+  float* final_norm_ = nullptr;
+  float* lm_head_ = nullptr;
+  std::vector<LayerWeights> layers_;
+
+  // [capacity][dim] / [capacity][hidden_dim] activations, fp32
+  int capacity_ = 0;
+  std::vector<std::shared_ptr<DeviceBuffer<float>>> activations_;
+  float* hidden_ = nullptr;
+  float* normed_ = nullptr;
+  float* q_ = nullptr;
+  float* k_ = nullptr;
+  float* v_ = nullptr;
+  float* attention_out_ = nullptr;
+  float* projected_ = nullptr;
+  float* gate_ = nullptr;
+  float* up_ = nullptr;
+  float* activated_ = nullptr;
+  std::shared_ptr<DeviceBuffer<int>> ids_;
+
+  std::shared_ptr<DeviceBuffer<float>> scores_;  // [num_heads][max_seq]
+  std::shared_ptr<DeviceBuffer<float>> logits_;  // [vocab]
+  std::shared_ptr<DeviceBuffer<float>> rope_table_;  // [max_seq][head_dim/2] (cos, sin)
+
+  bool verbose_ = false;
+};
+
+#endif  // EXECUTION_ENGINE_H

@@ -12,8 +12,8 @@ batched over rows and with the adds fused into the norms that follow them:
 The GEMMs between these ops are outside the path: their outputs (attn_out, q,
 k, v, ffn_out, gate, up) are inputs here. :data:`WORKLOADS` holds the token
 layouts and model shapes the kernels are measured on; :class:`LayerBuffers`
-allocates and seeds one step's device buffers; :func:`run_step` issues the five
-launches through the C ABI.
+allocates and seeds one step's device buffers; :func:`run_step` issues the
+launches through the C ABI (:func:`step_launchers` gives them one by one).
 """
 from __future__ import annotations
 
@@ -42,6 +42,7 @@ class LayerShape:
     eps: float = 1e-5
     positions: str = "tiled"  # "tiled": pos = r mod max_seq, seq = r // max_seq; "uniform": pos ~ U[0, max_seq)
     description: str = ""
+    kind: str = "layer"  # "layer": the five ops; "stress": Zipf-id gather + SwiGLU with +-20 outliers
 
     @property
     def es(self) -> int:
@@ -63,6 +64,8 @@ class LayerShape:
         """(kernel, algorithmic bytes per launch) in launch order for one step."""
         b = self.bytes_per_row()
         r = self.rows
+        if self.kind == "stress":
+            return [("embed_gather", b["embed_gather"] * r), ("swiglu", b["swiglu"] * r)]
         return [("embed_gather", b["embed_gather"] * r), ("add_rmsnorm_attn", b["add_rmsnorm"] * r),
                 ("rope_kv_store", b["rope_kv_store"] * r), ("add_rmsnorm_ffn", b["add_rmsnorm"] * r),
                 ("swiglu", b["swiglu"] * r)]
@@ -93,6 +96,11 @@ WORKLOADS = {
         "llama8b_prefill_bf16", rows=32768, dim=4096, hq=32, hkv=8, hd=128, ffn=14336, vocab=128256, theta=5e5,
         max_seq=8192, num_seqs=4, dtype=torch.bfloat16,
         description="Llama-3-8B prefill: 4 sequences x 8192 tokens"),
+    "swiglu_stress_bf16": LayerShape(
+        "swiglu_stress_bf16", rows=65536, dim=4096, hq=32, hkv=8, hd=128, ffn=14336, vocab=128256, theta=5e5,
+        max_seq=8192, num_seqs=8, dtype=torch.bfloat16, kind="stress",
+        description="SwiGLU stress: 65536 tokens x FFN 14336 with 1% of gate/up at +-20, and a gather of "
+                    "65536 Zipf(1.1) ids over vocab 128256 (dim 4096)"),
     "llama70b_bf16": LayerShape(
         "llama70b_bf16", rows=131072, dim=8192, hq=64, hkv=8, hd=128, ffn=28672, vocab=128256, theta=5e5,
         max_seq=8192, num_seqs=16, dtype=torch.bfloat16,
@@ -127,7 +135,14 @@ class LayerBuffers:
 
         R, D = s.rows, s.dim
         self.embed = randn(s.vocab, D, scale=0.02)
-        self.ids = torch.randint(0, s.vocab, (R,), generator=g, device=self.device, dtype=torch.int32)
+        if s.kind == "stress":
+            # Zipf(1.1) over the vocabulary by inverse CDF: heavy repeats of the first ids
+            rank = torch.arange(1, s.vocab + 1, device=self.device, dtype=torch.float64)
+            cdf = torch.cumsum(rank.pow(-1.1), 0)
+            u = torch.rand(R, generator=g, device=self.device, dtype=torch.float64) * cdf[-1]
+            self.ids = torch.searchsorted(cdf, u).clamp_(max=s.vocab - 1).to(torch.int32)
+        else:
+            self.ids = torch.randint(0, s.vocab, (R,), generator=g, device=self.device, dtype=torch.int32)
         if s.positions == "uniform":
             self.positions = torch.randint(0, s.max_seq, (R,), generator=g, device=self.device, dtype=torch.int32)
             self.seq_ids = (torch.arange(R, device=self.device, dtype=torch.int32) % s.num_seqs).contiguous()
@@ -150,42 +165,68 @@ class LayerBuffers:
         self.y_ffn = torch.empty(R, D, dtype=dt, device=self.device)
         self.gate = randn(R, s.ffn)
         self.up = randn(R, s.ffn)
+        if s.kind == "stress":  # 1% of entries at +-20: silu saturates on both sides
+            for t in (self.gate, self.up):
+                mask = torch.rand(t.shape, generator=g, device=self.device) < 0.01
+                sign = torch.where(torch.rand(t.shape, generator=g, device=self.device) < 0.5, -20.0, 20.0)
+                t[mask] = sign[mask].to(dt)
         self.act = torch.empty(R, s.ffn, dtype=dt, device=self.device)
         self.table = ops.RopeTable(s.max_seq, s.hd, s.theta, self.device) if with_table else None
         self.status = ops.DeviceStatus(self.device)
 
-    # tensors a host-buffer (end-to-end) call copies in and out each step
-    INPUTS = ("ids", "positions", "seq_ids", "attn_out", "q", "k", "v", "ffn_out", "gate", "up")
-    OUTPUTS = ("hidden", "y_attn", "q", "y_ffn", "act")
+    def inputs(self) -> tuple:
+        """Tensors an end-to-end (host-buffer) step copies in, every step."""
+        if self.shape.kind == "stress":
+            return ("ids", "gate", "up")
+        return ("ids", "positions", "seq_ids", "attn_out", "q", "k", "v", "ffn_out", "gate", "up")
+
+    def outputs(self) -> tuple:
+        """Tensors an end-to-end step copies back, every step (the KV cache stays on the device)."""
+        if self.shape.kind == "stress":
+            return ("hidden", "act")
+        return ("hidden", "y_attn", "q", "y_ffn", "act")
 
     def nbytes(self, names) -> int:
         return sum(getattr(self, n).numel() * getattr(self, n).element_size() for n in names)
 
 
-def run_step(b: LayerBuffers, stream: Optional[torch.cuda.Stream] = None, events: Optional[list] = None,
-             rows: Optional[slice] = None) -> int:
-    """Issues the step's five kernels on `stream` (default: the current stream).
-    With `events` (6 CUDA events), records one before the first and after each
-    launch. `rows` restricts the step to a contiguous row range (a chunk).
-    Returns the number of kernel launches."""
+def step_launchers(b: LayerBuffers, stream: Optional[torch.cuda.Stream] = None,
+                   rows: Optional[slice] = None) -> list:
+    """The step's kernels as (name, launch) pairs in order; each launch issues one
+    kernel on `stream` (default: the current stream). `rows` restricts the step
+    to a contiguous row range (a chunk). Names match LayerShape.step_kernels."""
     s = b.shape
     sl = rows if rows is not None else slice(0, s.rows)
-
-    def rec(i):
-        if events is not None:
-            events[i].record(stream)
-
     st = b.status
-    rec(0)
-    ops.embed_gather(b.embed, b.ids[sl], out=b.hidden[sl], status=st, stream=stream)
-    rec(1)
-    ops.add_rmsnorm(b.hidden[sl], b.attn_out[sl], b.w_attn, s.eps, out=b.y_attn[sl], stream=stream)
-    rec(2)
-    ops.rope_kv_store(b.q[sl], b.k[sl], b.v[sl], b.positions[sl], b.k_cache, b.v_cache, table=b.table,
-                      theta=s.theta, seq_ids=b.seq_ids[sl], status=st, stream=stream)
-    rec(3)
-    ops.add_rmsnorm(b.hidden[sl], b.ffn_out[sl], b.w_ffn, s.eps, out=b.y_ffn[sl], stream=stream)
-    rec(4)
-    ops.swiglu(b.gate[sl], b.up[sl], out=b.act[sl], stream=stream)
-    rec(5)
-    return 5
+    gather = ("embed_gather", lambda: ops.embed_gather(b.embed, b.ids[sl], out=b.hidden[sl], status=st,
+                                                        stream=stream))
+    swiglu = ("swiglu", lambda: ops.swiglu(b.gate[sl], b.up[sl], out=b.act[sl], stream=stream))
+    if s.kind == "stress":
+        return [gather, swiglu]
+    return [
+        gather,
+        ("add_rmsnorm_attn", lambda: ops.add_rmsnorm(b.hidden[sl], b.attn_out[sl], b.w_attn, s.eps,
+                                                     out=b.y_attn[sl], stream=stream)),
+        ("rope_kv_store", lambda: ops.rope_kv_store(b.q[sl], b.k[sl], b.v[sl], b.positions[sl], b.k_cache,
+                                                    b.v_cache, table=b.table, theta=s.theta,
+                                                    seq_ids=b.seq_ids[sl], status=st, stream=stream)),
+        ("add_rmsnorm_ffn", lambda: ops.add_rmsnorm(b.hidden[sl], b.ffn_out[sl], b.w_ffn, s.eps,
+                                                    out=b.y_ffn[sl], stream=stream)),
+        swiglu,
+    ]
+
+
+def run_step(b: LayerBuffers, stream: Optional[torch.cuda.Stream] = None, events: Optional[list] = None,
+             rows: Optional[slice] = None) -> int:
+    """Issues the step's kernels on `stream` (default: the current stream). With
+    `events` (one more than the launches), records one before the first launch
+    and one after each. `rows` restricts the step to a row range. Returns the
+    number of kernel launches."""
+    launchers = step_launchers(b, stream, rows)
+    if events is not None:
+        events[0].record(stream)
+    for i, (_, launch) in enumerate(launchers):
+        launch()
+        if events is not None:
+            events[i + 1].record(stream)
+    return len(launchers)

@@ -42,6 +42,9 @@ sys.path.insert(0, REPO)
 
 METRIC = "achieved HBM GB/s and % of B200 peak per fused layer kernel; rows/s at 1/2/4/8 GPUs"
 FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126 * 2**20
+L2_RESIDENT_BYTES = 4 * L2_BYTES  # a step moving less than this would be served from L2 when repeated
+L2_FLUSH_BYTES = 256 * 2**20
 
 
 def log(*a):
@@ -206,6 +209,7 @@ def make_host_step(shape, rows: int, seed: int = 0):
     st.hq, st.hkv, st.hd, st.max_seq, st.num_seqs, st.table_len = (shape.hq, shape.hkv, shape.hd, shape.max_seq,
                                                                    shape.num_seqs, 0)
     st.eps, st.theta, st.dtype = shape.eps, shape.theta, 1 if is_bf16 else 0
+    st.ops = 1 | 16 if shape.kind == "stress" else 0  # stress: gather + SwiGLU; else all five ops
     for name, arr in bufs.items():
         setattr(st, name, arr.ctypes.data)
     return st, bufs
@@ -301,7 +305,8 @@ def config_dict(shape, n):
             "head_dim": shape.hd, "ffn": shape.ffn, "vocab": shape.vocab, "rope_theta": shape.theta,
             "max_seq": shape.max_seq, "sequences_per_gpu": shape.num_seqs,
             "l2": f"inputs larger than L2: {shape.step_bytes() / 1e9:.2f} GB moved per step vs 126 MB L2"
-                  if shape.step_bytes() > 4 * 126e6 else "L2 not flushed: working set is L2-resident",
+                  if shape.step_bytes() >= L2_RESIDENT_BYTES else
+                  "L2 flushed (256 MB write) before every kernel; each kernel replayed as a one-launch CUDA graph",
             "parallelism": f"rows{n}: tokens partitioned across {n} GPU(s), no collectives"}
 
 
@@ -357,20 +362,56 @@ def main() -> int:
     stream.synchronize()
     assert b.status.read(stream) == 0, "device status set during warm-up"
 
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)] for _ in range(K)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    small = shape.step_bytes() < L2_RESIDENT_BYTES
     launches = 0
-    barrier()
-    torch.cuda.synchronize(dev)
-    with ClockSampler(dev) as clocks:
-        start.record(stream)
-        for i in range(K):
-            launches += layer.run_step(b, stream, events[i])
-        end.record(stream)
+    if not small:
+        # Inputs far larger than L2: K back-to-back steps, events between launches.
+        events = [[torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)] for _ in range(K)]
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
         torch.cuda.synchronize(dev)
-    barrier()
-    elapsed_ms = start.elapsed_time(end)
-    per_kernel = [statistics.mean(events[i][j].elapsed_time(events[i][j + 1]) for i in range(K)) for j in range(nk)]
+        with ClockSampler(dev) as clocks:
+            start.record(stream)
+            for i in range(K):
+                launches += layer.run_step(b, stream, events[i])
+            end.record(stream)
+            torch.cuda.synchronize(dev)
+        barrier()
+        elapsed_ms = start.elapsed_time(end)
+        per_kernel = [statistics.mean(events[i][j].elapsed_time(events[i][j + 1]) for i in range(K))
+                      for j in range(nk)]
+    else:
+        # An L2-resident working set: every kernel runs as a CUDA graph of that one
+        # launch (no host launch cost in the measurement), after a 256 MB write that
+        # evicts L2; the step time is the sum of the kernels' event times.
+        flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        graphs = []
+        for _, launch in layer.step_launchers(b):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                launch()
+            graphs.append(g)
+        ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(nk)]
+              for _ in range(K)]
+        with torch.cuda.stream(stream):
+            for _ in range(W):
+                for g in graphs:
+                    flush.zero_()
+                    g.replay()
+            barrier()
+            torch.cuda.synchronize(dev)
+            with ClockSampler(dev) as clocks:
+                for i in range(K):
+                    for j, g in enumerate(graphs):
+                        flush.zero_()
+                        ev[i][j][0].record(stream)
+                        g.replay()
+                        ev[i][j][1].record(stream)
+                        launches += 1
+                torch.cuda.synchronize(dev)
+        barrier()
+        per_kernel = [statistics.mean(ev[i][j][0].elapsed_time(ev[i][j][1]) for i in range(K)) for j in range(nk)]
+        elapsed_ms = sum(per_kernel) * K
     assert b.status.read(stream) == 0, "device status set during the timed steps"
     res = max_over_ranks([elapsed_ms] + per_kernel)
     elapsed_ms, per_kernel = res[0], res[1:]
@@ -479,7 +520,7 @@ def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
 
     from baremetalinferenceengine_b200 import layer
 
-    names_in, names_out = layer.LayerBuffers.INPUTS, layer.LayerBuffers.OUTPUTS
+    names_in, names_out = b.inputs(), b.outputs()
     io_per_row = (b.nbytes(names_in) + b.nbytes(names_out)) / shape.rows
     try:
         import psutil

@@ -24,8 +24,8 @@
  *                       k and v (src/execution_engine.cu:113-115)
  *   oracle_gather       the row copy of src/execution_engine.cu:98-99 with the
  *                       id check of src/execution_engine.cu:63-65
- *   oracle_layer_step(_mt)  the five ops above over a row range, single- or
- *                       multi-threaded: the timed CPU baseline.
+ *   oracle_layer_step(_mt)  the five ops above (or a chosen subset) over a row
+ *                       range, single- or multi-threaded: the timed CPU baseline.
  */
 #include <math.h>
 #include <pthread.h>
@@ -299,17 +299,25 @@ typedef struct OracleStep {
   const void* gate;      /* [rows][ffn] */
   const void* up;        /* [rows][ffn] */
   void* act;             /* [rows][ffn] */
+  int32_t ops;           /* bit mask of the ops to run: 1 gather, 2 attention add+RMSNorm, 4 RoPE+KV,
+                            8 FFN add+RMSNorm, 16 SwiGLU (0 = all five) */
 } OracleStep;
 
 int32_t oracle_layer_step(const OracleStep* s, int64_t r0, int64_t r1) {
   const size_t es = esize(s->dtype);
-  int32_t bad = gather_rows(s->hidden, s->embed, s->ids, r0, r1, s->dim, s->vocab, s->dim, s->dtype);
-  add_rmsnorm_rows(s->hidden, s->attn_out, s->w_attn, s->normed, r0, r1, s->dim, s->eps, s->dtype);
-  bad |= rope_kv_rows(s->q, s->k, s->v, s->positions, 0, s->seq_ids, s->k_cache, s->v_cache, s->table_len,
-                      s->theta, r0, r1, s->hq, s->hkv, s->hd, s->max_seq, s->num_seqs, s->dtype);
-  add_rmsnorm_rows(s->hidden, s->ffn_out, s->w_ffn, s->normed, r0, r1, s->dim, s->eps, s->dtype);
-  oracle_swiglu((char*)s->act + r0 * s->ffn * es, (const char*)s->gate + r0 * s->ffn * es,
-                (const char*)s->up + r0 * s->ffn * es, (r1 - r0) * s->ffn, s->dtype);
+  const int32_t ops = s->ops ? s->ops : 31;
+  int32_t bad = 0;
+  if (ops & 1) bad |= gather_rows(s->hidden, s->embed, s->ids, r0, r1, s->dim, s->vocab, s->dim, s->dtype);
+  if (ops & 2) add_rmsnorm_rows(s->hidden, s->attn_out, s->w_attn, s->normed, r0, r1, s->dim, s->eps, s->dtype);
+  if (ops & 4) {
+    bad |= rope_kv_rows(s->q, s->k, s->v, s->positions, 0, s->seq_ids, s->k_cache, s->v_cache, s->table_len,
+                        s->theta, r0, r1, s->hq, s->hkv, s->hd, s->max_seq, s->num_seqs, s->dtype);
+  }
+  if (ops & 8) add_rmsnorm_rows(s->hidden, s->ffn_out, s->w_ffn, s->normed, r0, r1, s->dim, s->eps, s->dtype);
+  if (ops & 16) {
+    oracle_swiglu((char*)s->act + r0 * s->ffn * es, (const char*)s->gate + r0 * s->ffn * es,
+                  (const char*)s->up + r0 * s->ffn * es, (r1 - r0) * s->ffn, s->dtype);
+  }
   return bad;
 }
 

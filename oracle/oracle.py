@@ -44,6 +44,7 @@ class OracleStep(ctypes.Structure):
         ("ids", vp), ("embed", vp), ("hidden", vp), ("attn_out", vp), ("w_attn", vp), ("normed", vp),
         ("q", vp), ("k", vp), ("v", vp), ("positions", vp), ("seq_ids", vp), ("k_cache", vp), ("v_cache", vp),
         ("ffn_out", vp), ("w_ffn", vp), ("gate", vp), ("up", vp), ("act", vp),
+        ("ops", i32),
     ]
 
 
