@@ -52,6 +52,19 @@ SIGNATURES = {
                         c_int32, c_int32, c_int, c_void_p, c_void_p]),
     "bm_kv_store": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_int64, c_int32, c_int32, c_int32,
                             c_int32, c_int, c_void_p, c_void_p]),
+    "bm_decode_attention_workspace_size": (c_int, [c_int64, c_int32, c_int32, c_int32, c_int32,
+                                                   ctypes.POINTER(ctypes.c_size_t)]),
+    "bm_decode_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int64,
+                                    c_int32, c_int32, c_int32, c_int32, c_int32, c_float, c_void_p, ctypes.c_size_t,
+                                    c_int, c_void_p, c_void_p]),
+    "bm_kv_cache_create": (c_int, [c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_int,
+                                   ctypes.POINTER(c_void_p)]),
+    "bm_kv_cache_destroy": (c_int, [c_void_p]),
+    "bm_kv_cache_layer": (c_int, [c_void_p, c_int32, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p)]),
+    "bm_kv_cache_seq_len": (c_int, [c_void_p, c_int32, P_INT32]),
+    "bm_kv_cache_reset": (c_int, [c_void_p, c_int32]),
+    "bm_kv_cache_append": (c_int, [c_void_p, c_void_p, c_int64, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p),
+                                   c_void_p]),
 }
 
 _lock = threading.Lock()

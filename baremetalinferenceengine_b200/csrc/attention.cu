@@ -1,0 +1,441 @@
+// Decode attention over the static KV cache: one query token per entry, GQA.
+//
+// Reference semantics (src/kernels.cu:225-264): for one token and each head h,
+//   scores[j] = dot(q[h], k_cache[h][j]) * rsqrt(head_dim), j < seq_len;
+//   w = softmax(scores);  out[h][d] = sum_j w[j] * v_cache[h][j][d]
+// as three launches (scores, softmax, mix), one block per head, fp32, batch 1.
+//
+// Here a batch of queries (query b reads cache sequence seq_ids[b] over positions
+// [0, lens[b])) runs in one launch, q head h reading kv head h / G where
+// G = num_q_heads / num_kv_heads (GQA), fp32 or bf16 cache. The sequence is cut
+// into splits of S positions; one CTA of 128 threads takes (query, kv head,
+// split) and processes it in tiles of 128 positions:
+//   scores: thread t dots position t's K row (16-byte loads) with the G queries
+//           of the group, held pre-scaled (by log2(e) / sqrt(head_dim)) in
+//           shared memory;
+//   softmax: running max and sum per query, base-2 exponentials (exp2f), tile
+//           maxima and sums by warp shuffles plus a shared-memory pass;
+//   mix:    warp w takes positions w, w+4, ...; lane l owns dimensions
+//           l, l+32, ... and accumulates p * V for the G queries.
+// The four warps' accumulators are summed through shared memory at the end.
+// With one split the CTA writes the normalised output; with several it writes
+// (max, sum, unnormalised output) per query to the workspace and
+// attention_combine_kernel merges the splits.
+#include <algorithm>
+#include <cmath>
+
+#include "bm_common.cuh"
+#include "bm_host.h"
+
+namespace bm {
+namespace {
+
+constexpr int kThreads = 128;  // = positions per tile
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxGroup = 16;
+constexpr int kMaxHeadDim = 256;
+
+struct AttnArgs {
+  void* out;              // [batch][hq][hd]
+  const void* q;          // [batch][hq][hd]
+  const void* k_cache;    // [num_seqs][hkv][max_seq][hd]
+  const void* v_cache;
+  const int32_t* seq_ids; // NULL: 0
+  const int32_t* lens;    // NULL: len0 for every query
+  int32_t len0;
+  int64_t batch;
+  int hq, hkv, hd, group, max_seq, num_seqs;
+  int splits, split_len;  // positions per split (a multiple of kThreads)
+  float qscale;           // log2(e) * softmax scale
+  float* ws;              // [batch][hkv][splits][group][hd + 2]: o..., m, l
+  int32_t* status;
+};
+
+__device__ __forceinline__ int query_len(const AttnArgs& a, int64_t b) { return a.lens ? a.lens[b] : a.len0; }
+
+// Returns the query's status bits (0 = valid).
+__device__ __forceinline__ int32_t check_query(const AttnArgs& a, int64_t b, int* seq, int* len) {
+  *seq = a.seq_ids ? a.seq_ids[b] : 0;
+  *len = query_len(a, b);
+  int32_t bad = 0;
+  if (*seq < 0 || *seq >= a.num_seqs) bad |= BM_DEVERR_BAD_SEQUENCE;
+  if (*len <= 0 || *len > a.max_seq) bad |= BM_DEVERR_BAD_POSITION;
+  return bad;
+}
+
+// Block-wide max or sum of G values per thread (vals[g]); every thread gets the results.
+// (Loops run to the compile-time GM so the register array is never indexed at run time.)
+template <bool MAX, int GM>
+__device__ __forceinline__ void block_reduce(float (&vals)[GM], int G, float (*scratch)[kMaxGroup]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int g = 0; g < GM; ++g) {
+    if (g < G) {
+      float v = vals[g];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const float o = __shfl_xor_sync(0xffffffffu, v, off);
+        v = MAX ? fmaxf(v, o) : v + o;
+      }
+      if (lane == 0) scratch[warp][g] = v;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < GM; ++g) {
+    if (g < G) {
+      float v = scratch[0][g];
+#pragma unroll
+      for (int w = 1; w < kWarps; ++w) v = MAX ? fmaxf(v, scratch[w][g]) : v + scratch[w][g];
+      vals[g] = v;
+    }
+  }
+  __syncthreads();
+}
+
+// GM: the group size rounded up to a power of two (register arrays are sized by
+// it); DPL = ceil(head_dim / 32): lane l owns dimensions l, l + 32, ... of the mix.
+template <typename T, int GM, int DPL>
+__global__ void __launch_bounds__(kThreads) attention_split_kernel(AttnArgs a) {
+  constexpr int VEC = VecWidth<T>::value;
+  extern __shared__ float smem[];
+  // layout: q_s [G][hd] | p_s [G][kThreads] | red [kWarps][G][hd]
+  const int G = a.group, hd = a.hd;
+  float* q_s = smem;
+  float* p_s = q_s + G * hd;
+  float* red = p_s + G * kThreads;
+  __shared__ float scratch[kWarps][kMaxGroup];
+  __shared__ float m_s[kMaxGroup], l_s[kMaxGroup], alpha_s[kMaxGroup];
+
+  const int64_t b = blockIdx.z;
+  const int kvh = blockIdx.y;
+  const int split = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int seq, len;
+  const int32_t bad = check_query(a, b, &seq, &len);
+  if (bad) {  // uniform: every thread of the CTA read the same query
+    if (tid == 0 && kvh == 0 && split == 0) raise_status(a.status, bad);
+    return;
+  }
+  const int start = split * a.split_len;
+  const int end = min(len, start + a.split_len);
+  float* ws = a.ws ? a.ws + (((b * a.hkv + kvh) * a.splits + split) * G) * static_cast<int64_t>(hd + 2) : nullptr;
+  if (start >= end) {  // this split lies past the query's length: an empty partial
+    if (ws != nullptr && tid < G) {
+      ws[tid * (hd + 2) + hd] = -INFINITY;
+      ws[tid * (hd + 2) + hd + 1] = 0.f;
+    }
+    return;
+  }
+
+  // queries of the group, pre-scaled, in shared memory
+  const T* qb = static_cast<const T*>(a.q) + (b * a.hq + static_cast<int64_t>(kvh) * G) * hd;
+  for (int i = tid; i < G * hd; i += kThreads) q_s[i] = load1<T>(qb + i) * a.qscale;
+  if (tid < G) {
+    m_s[tid] = -INFINITY;
+    l_s[tid] = 0.f;
+  }
+  const int64_t head_base = (static_cast<int64_t>(seq) * a.hkv + kvh) * a.max_seq * hd;
+  const T* kbase = static_cast<const T*>(a.k_cache) + head_base;
+  const T* vbase = static_cast<const T*>(a.v_cache) + head_base;
+
+  float acc[GM][DPL];
+#pragma unroll
+  for (int g = 0; g < GM; ++g)
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) acc[g][i] = 0.f;
+  __syncthreads();
+
+  for (int tile = start; tile < end; tile += kThreads) {
+    const int p = tile + tid;
+    float s[GM];
+#pragma unroll
+    for (int g = 0; g < GM; ++g) s[g] = 0.f;
+    if (p < end) {
+      const T* krow = kbase + static_cast<int64_t>(p) * hd;
+      for (int c = 0; c < hd; c += VEC) {
+        float k[VEC];
+        unpack16<T>(__ldg(reinterpret_cast<const uint4*>(krow + c)), k);
+#pragma unroll
+        for (int g = 0; g < GM; ++g) {
+          if (g < G) {
+            float dot = s[g];
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) dot = fmaf(q_s[g * hd + c + e], k[e], dot);
+            s[g] = dot;
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int g = 0; g < GM; ++g) s[g] = -INFINITY;
+    }
+    // online softmax (base 2): tile max, rescale factors, probabilities, tile sum
+    float t[GM];
+#pragma unroll
+    for (int g = 0; g < GM; ++g) t[g] = s[g];
+    block_reduce<true, GM>(t, G, scratch);
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      if (g < G) {
+        const float m_new = fmaxf(m_s[g], t[g]);
+        const float pr = (p < end) ? exp2f(s[g] - m_new) : 0.f;
+        p_s[g * kThreads + tid] = pr;
+        t[g] = pr;
+        s[g] = m_new;  // reuse: the new running max
+      }
+    }
+    block_reduce<false, GM>(t, G, scratch);  // tile sums; its barriers also publish p_s
+    float m_mine = 0.f, sum_mine = 0.f;  // thread g < G updates query g's running state
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      if (g == tid) {
+        m_mine = s[g];
+        sum_mine = t[g];
+      }
+    }
+    if (tid < G) {
+      const float alpha = exp2f(m_s[tid] - m_mine);
+      alpha_s[tid] = alpha;
+      l_s[tid] = l_s[tid] * alpha + sum_mine;
+      m_s[tid] = m_mine;
+    }
+    __syncthreads();
+    // mix: rescale, then accumulate p * V over this warp's positions of the tile
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      if (g < G) {
+        const float al = alpha_s[g];
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[g][i] *= al;
+      }
+    }
+    const int tile_end = min(end - tile, kThreads);
+    for (int j = warp; j < tile_end; j += kWarps) {
+      const T* vrow = vbase + static_cast<int64_t>(tile + j) * hd;
+      float v[DPL];
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) {
+        const int d = lane + 32 * i;
+        v[i] = d < hd ? load1<T>(vrow + d) : 0.f;
+      }
+#pragma unroll
+      for (int g = 0; g < GM; ++g) {
+        if (g < G) {
+          const float pr = p_s[g * kThreads + j];
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) acc[g][i] = fmaf(pr, v[i], acc[g][i]);
+        }
+      }
+    }
+    __syncthreads();  // p_s, alpha_s are rewritten by the next tile
+  }
+
+  // sum the warps' accumulators
+#pragma unroll
+  for (int g = 0; g < GM; ++g) {
+    if (g < G) {
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) {
+        const int d = lane + 32 * i;
+        if (d < hd) red[(warp * G + g) * hd + d] = acc[g][i];
+      }
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < G * hd; i += kThreads) {
+    float o = red[i];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) o += red[w * G * hd + i];
+    const int g = i / hd, d = i - g * hd;
+    if (ws == nullptr) {
+      T* out = static_cast<T*>(a.out) + (b * a.hq + static_cast<int64_t>(kvh) * G + g) * hd;
+      store1<T>(out + d, o / l_s[g]);
+    } else {
+      ws[g * (hd + 2) + d] = o;
+      if (d == 0) {
+        ws[g * (hd + 2) + hd] = m_s[g];
+        ws[g * (hd + 2) + hd + 1] = l_s[g];
+      }
+    }
+  }
+}
+
+// One CTA per (query, q head): merges the splits' (max, sum, output) partials.
+template <typename T>
+__global__ void __launch_bounds__(256) attention_combine_kernel(AttnArgs a) {
+  const int64_t b = blockIdx.y;
+  const int h = blockIdx.x;
+  int seq, len;
+  if (check_query(a, b, &seq, &len)) return;  // reported by the split kernel
+  const int kvh = h / a.group, g = h - kvh * a.group;
+  const int hd = a.hd;
+  const float* base = a.ws + ((b * a.hkv + kvh) * a.splits * a.group + g) * static_cast<int64_t>(hd + 2);
+  const int64_t split_stride = static_cast<int64_t>(a.group) * (hd + 2);
+  float m = -INFINITY;
+  for (int s = 0; s < a.splits; ++s) m = fmaxf(m, base[s * split_stride + hd]);
+  float l = 0.f;
+  for (int s = 0; s < a.splits; ++s) {
+    const float ms = base[s * split_stride + hd];
+    if (ms != -INFINITY) l += base[s * split_stride + hd + 1] * exp2f(ms - m);
+  }
+  T* out = static_cast<T*>(a.out) + (b * a.hq + h) * hd;
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float o = 0.f;
+    for (int s = 0; s < a.splits; ++s) {
+      const float ms = base[s * split_stride + hd];
+      if (ms != -INFINITY) o += base[s * split_stride + d] * exp2f(ms - m);
+    }
+    store1<T>(out + d, o / l);
+  }
+}
+
+// Splits for `pairs` (query, kv head) pairs over at most max_len positions:
+// enough CTAs to fill the GPU several times, each split a whole number of tiles.
+void plan_splits(int64_t pairs, int max_len, int sms, int* splits, int* split_len) {
+  const int tiles = (max_len + kThreads - 1) / kThreads;
+  const int64_t want = std::max<int64_t>(1, (static_cast<int64_t>(sms) * 4 + pairs - 1) / pairs);
+  const int n = static_cast<int>(std::min<int64_t>(want, tiles));
+  const int tiles_per_split = (tiles + n - 1) / n;
+  *split_len = tiles_per_split * kThreads;
+  *splits = (tiles + tiles_per_split - 1) / tiles_per_split;
+}
+
+size_t workspace_bytes(int64_t batch, int hkv, int group, int hd, int splits) {
+  return splits <= 1 ? 0 : static_cast<size_t>(batch) * hkv * splits * group * (hd + 2) * sizeof(float);
+}
+
+int check_args(const char* what, int64_t batch, int hq, int hkv, int hd, int max_seq, int num_seqs, int max_len,
+               bm_dtype_t dtype) {
+  if (!valid_dtype(dtype)) return fail(BM_ERR_INVALID_ARGUMENT, "%s: bad dtype", what);
+  if (batch < 0 || batch > 65535) return fail(BM_ERR_INVALID_ARGUMENT, "%s: batch outside [0, 65535]", what);
+  if (hq <= 0 || hkv <= 0 || hq % hkv != 0 || hq / hkv > kMaxGroup || hkv > 65535) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: need num_q_heads a multiple of num_kv_heads, at most %d per kv head",
+                what, kMaxGroup);
+  }
+  if (hd <= 0 || hd > kMaxHeadDim || (hd * dtype_size(dtype)) % 16 != 0) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: head_dim rows must be whole 16-byte vectors, head_dim <= %d", what,
+                kMaxHeadDim);
+  }
+  if (max_seq <= 0 || num_seqs <= 0) return fail(BM_ERR_INVALID_ARGUMENT, "%s: bad max_seq or num_seqs", what);
+  if (max_len <= 0 || max_len > max_seq) return fail(BM_ERR_INVALID_ARGUMENT, "%s: max_len outside [1, max_seq]", what);
+  return BM_OK;
+}
+
+template <typename T, int GM>
+int launch_group(const AttnArgs& a, size_t smem, cudaStream_t stream) {
+  const dim3 grid(a.splits, a.hkv, static_cast<unsigned>(a.batch));
+  auto go = [&](auto kernel) {
+    if (smem > 48 * 1024) {
+      cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (err != cudaSuccess) return fail(BM_ERR_CUDA, "bm_decode_attention: %s", cudaGetErrorString(err));
+    }
+    kernel<<<grid, kThreads, smem, stream>>>(a);
+    return check_launch("bm_decode_attention");
+  };
+  switch ((a.hd + 31) / 32) {
+    case 1: return go(attention_split_kernel<T, GM, 1>);
+    case 2: return go(attention_split_kernel<T, GM, 2>);
+    case 3: return go(attention_split_kernel<T, GM, 3>);
+    case 4: return go(attention_split_kernel<T, GM, 4>);
+    case 5: return go(attention_split_kernel<T, GM, 5>);
+    case 6: return go(attention_split_kernel<T, GM, 6>);
+    case 7: return go(attention_split_kernel<T, GM, 7>);
+    default: return go(attention_split_kernel<T, GM, 8>);
+  }
+}
+
+template <typename T>
+int launch(AttnArgs a, cudaStream_t stream) {
+  const size_t smem = sizeof(float) * (static_cast<size_t>(a.group) * a.hd + a.group * kThreads +
+                                       static_cast<size_t>(kWarps) * a.group * a.hd);
+  int st;
+  if (a.group <= 1) {
+    st = launch_group<T, 1>(a, smem, stream);
+  } else if (a.group <= 2) {
+    st = launch_group<T, 2>(a, smem, stream);
+  } else if (a.group <= 4) {
+    st = launch_group<T, 4>(a, smem, stream);
+  } else if (a.group <= 8) {
+    st = launch_group<T, 8>(a, smem, stream);
+  } else {
+    st = launch_group<T, 16>(a, smem, stream);
+  }
+  if (st != BM_OK || a.splits == 1) return st;
+  attention_combine_kernel<T><<<dim3(a.hq, static_cast<unsigned>(a.batch)), std::min(256, a.hd), 0, stream>>>(a);
+  return check_launch("bm_decode_attention (combine)");
+}
+
+}  // namespace
+
+int decode_attention(void* out, const void* q, const void* k_cache, const void* v_cache, const int32_t* seq_ids,
+                     const int32_t* lens, int32_t len0, int32_t max_len, int64_t batch, int32_t hq, int32_t hkv,
+                     int32_t hd, int32_t max_seq, int32_t num_seqs, float scale, void* workspace,
+                     size_t workspace_size, bm_dtype_t dtype, int32_t* d_status, void* stream) {
+  const char* what = "bm_decode_attention";
+  if (int st = check_args(what, batch, hq, hkv, hd, max_seq, num_seqs, max_len, dtype)) return st;
+  if (batch == 0) return BM_OK;
+  if (!out || !q || !k_cache || !v_cache) return fail(BM_ERR_INVALID_ARGUMENT, "%s: NULL pointer", what);
+  const int es = dtype_size(dtype);
+  if (!aligned16(k_cache) || !aligned16(v_cache) || (hd * es) % 16 != 0) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: caches must be 16-byte aligned", what);
+  }
+  if (!(scale > 0.f)) scale = 1.0f / sqrtf(static_cast<float>(hd));
+  AttnArgs a{};
+  a.out = out;
+  a.q = q;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.seq_ids = seq_ids;
+  a.lens = lens;
+  a.len0 = len0;
+  a.batch = batch;
+  a.hq = hq;
+  a.hkv = hkv;
+  a.hd = hd;
+  a.group = hq / hkv;
+  a.max_seq = max_seq;
+  a.num_seqs = num_seqs;
+  a.qscale = scale * 1.4426950408889634f;  // scores in base 2: exp(x) = exp2(x * log2(e))
+  a.status = d_status;
+  plan_splits(batch * hkv, max_len, sm_count(), &a.splits, &a.split_len);
+  const size_t need = workspace_bytes(batch, hkv, a.group, hd, a.splits);
+  if (need > 0 && (workspace == nullptr || workspace_size < need)) {
+    // Less scratch than the plan wants: as many splits as it holds (maybe one).
+    const size_t per_split = workspace_bytes(batch, hkv, a.group, hd, 2) / 2;
+    const int fit = workspace == nullptr ? 1 : static_cast<int>(std::min<size_t>(workspace_size / per_split, a.splits));
+    const int tiles = (max_len + kThreads - 1) / kThreads;
+    const int tiles_per_split = (tiles + std::max(fit, 1) - 1) / std::max(fit, 1);
+    a.split_len = tiles_per_split * kThreads;
+    a.splits = (tiles + tiles_per_split - 1) / tiles_per_split;
+  }
+  a.ws = a.splits > 1 ? static_cast<float*>(workspace) : nullptr;
+  cudaStream_t s = as_stream(stream);
+  return dtype == BM_F32 ? launch<float>(a, s) : launch<bf16>(a, s);
+}
+
+size_t decode_attention_workspace(int64_t batch, int32_t hq, int32_t hkv, int32_t hd, int32_t max_len) {
+  if (batch <= 0 || hkv <= 0 || hq % hkv != 0 || max_len <= 0) return 0;
+  int splits = 1, split_len = 0;
+  plan_splits(batch * hkv, max_len, sm_count(), &splits, &split_len);
+  return workspace_bytes(batch, hkv, hq / hkv, hd, splits);
+}
+
+}  // namespace bm
+
+extern "C" int bm_decode_attention_workspace_size(int64_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                                  int32_t head_dim, int32_t max_len, size_t* bytes_out) {
+  if (!bytes_out) return bm::fail(BM_ERR_INVALID_ARGUMENT, "bm_decode_attention_workspace_size: NULL bytes_out");
+  *bytes_out = bm::decode_attention_workspace(batch, num_q_heads, num_kv_heads, head_dim, max_len);
+  return BM_OK;
+}
+
+extern "C" int bm_decode_attention(void* out, const void* q, const void* k_cache, const void* v_cache,
+                                   const int32_t* seq_ids, const int32_t* lens, int32_t max_len, int64_t batch,
+                                   int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t max_seq,
+                                   int32_t num_seqs, float scale, void* workspace, size_t workspace_bytes,
+                                   bm_dtype_t dtype, int32_t* d_status, void* stream) {
+  if (!lens) return bm::fail(BM_ERR_INVALID_ARGUMENT, "bm_decode_attention: NULL lens");
+  return bm::decode_attention(out, q, k_cache, v_cache, seq_ids, lens, 0, max_len, batch, num_q_heads, num_kv_heads,
+                              head_dim, max_seq, num_seqs, scale, workspace, workspace_bytes, dtype, d_status, stream);
+}

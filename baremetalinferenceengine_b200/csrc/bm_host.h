@@ -29,4 +29,11 @@ inline bool valid_dtype(int dt) { return dt == BM_F32 || dt == BM_BF16; }
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// bm_decode_attention with a host-side length for every query (lens == NULL:
+// len0), as the reference's single-token launch_attention needs.
+int decode_attention(void* out, const void* q, const void* k_cache, const void* v_cache, const int32_t* seq_ids,
+                     const int32_t* lens, int32_t len0, int32_t max_len, int64_t batch, int32_t hq, int32_t hkv,
+                     int32_t hd, int32_t max_seq, int32_t num_seqs, float scale, void* workspace,
+                     size_t workspace_size, bm_dtype_t dtype, int32_t* d_status, void* stream);
+
 }  // namespace bm

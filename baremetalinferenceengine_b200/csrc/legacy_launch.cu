@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <cstdlib>
 
+#include "bm_host.h"
 #include "bm_layer_ops.h"
 #include "kernels.cuh"
 
@@ -69,4 +70,22 @@ void launch_kv_store(float* cache, float* src, int seq_pos, int num_heads, int h
   BM_LAUNCH_CHECK(bm_kv_store(cache, src, nullptr, seq_pos, nullptr, 1, num_heads, head_dim, max_seq_len, 1,
                               BM_F32, nullptr, stream),
                   "launch_kv_store");
+}
+
+// Reference: include/kernels.cuh:41, src/kernels.cu:258-264. One token, num_heads
+// query heads over as many kv heads, positions [0, seq_len) of a cache laid out
+// [num_heads][max_seq_len][head_dim]. The reference API hands its kernels
+// `scores` (at least num_heads * seq_len floats) as scratch; here it holds the
+// per-split partial results when the sequence is split across CTAs (as many
+// splits as fit in it), so the call allocates nothing.
+void launch_attention(float* out, float* q, float* k_cache, float* v_cache, float* scores, int num_heads,
+                      int head_dim, int max_seq_len, int seq_len, cudaStream_t stream) {
+  if (seq_len <= 0 || seq_len > max_seq_len) {
+    BM_LAUNCH_CHECK(BM_ERR_INVALID_ARGUMENT, "launch_attention (seq_len outside [1, max_seq_len])");
+  }
+  const size_t scratch = scores ? sizeof(float) * static_cast<size_t>(num_heads) * seq_len : 0;
+  BM_LAUNCH_CHECK(bm::decode_attention(out, q, k_cache, v_cache, nullptr, nullptr, seq_len, seq_len, 1, num_heads,
+                                       num_heads, head_dim, max_seq_len, 1, 0.f, scores, scratch, BM_F32, nullptr,
+                                       stream),
+                  "launch_attention");
 }

@@ -32,7 +32,6 @@ ExecutionEngine::ExecutionEngine(std::shared_ptr<MemoryAllocator> allocator, std
                        weight(p + "mlp.down_proj.weight")});
   }
   const int max_seq = kv_cache_->get_max_seq_len();
-  scores_ = std::make_shared<DeviceBuffer<float>>(static_cast<size_t>(config_.num_heads) * max_seq);
   logits_ = std::make_shared<DeviceBuffer<float>>(config_.vocab_size);
   // (cos, sin) per position, computed once on the device in fp64 and kept in L2-sized fp32
   rope_table_ = std::make_shared<DeviceBuffer<float>>(static_cast<size_t>(max_seq) * config_.head_dim());
@@ -70,6 +69,12 @@ void ExecutionEngine::reserve(int tokens) {
   up_ = buffer(n * hidden);
   activated_ = buffer(n * hidden);
   ids_ = std::make_shared<DeviceBuffer<int>>(n);
+  lens_ = std::make_shared<DeviceBuffer<int>>(n);
+  size_t ws = 0;
+  check(bm_decode_attention_workspace_size(tokens, config_.num_heads, config_.num_heads, config_.head_dim(),
+                                           kv_cache_->get_max_seq_len(), &ws),
+        "bm_decode_attention_workspace_size");
+  attention_workspace_ = std::make_shared<DeviceBuffer<char>>(ws);
   capacity_ = tokens;
 }
 
@@ -100,6 +105,10 @@ std::vector<float> ExecutionEngine::forward(const std::vector<int>& input_tokens
   const float eps = config_.norm_eps;
 
   CUDA_CHECK(cudaMemcpy(ids_->get(), input_tokens.data(), sizeof(int) * T, cudaMemcpyHostToDevice));
+  // token t attends to the positions up to its own: pos0 + t + 1 of them
+  std::vector<int> lens(T);
+  for (int t = 0; t < T; ++t) lens[t] = pos0 + t + 1;
+  CUDA_CHECK(cudaMemcpy(lens_->get(), lens.data(), sizeof(int) * T, cudaMemcpyHostToDevice));
   check(bm_embed_gather(hidden_, token_embeddings_, ids_->get(), T, dim, config_.vocab_size, dim, BM_F32, nullptr,
                         nullptr),
         "bm_embed_gather");
@@ -123,11 +132,11 @@ std::vector<float> ExecutionEngine::forward(const std::vector<int>& input_tokens
     check(bm_rope_kv_store(q_, k_, v_, nullptr, pos0, nullptr, k_cache, v_cache, rope_table_->get(), max_seq,
                            config_.rope_theta, T, heads, heads, head_dim, max_seq, 1, BM_F32, nullptr, nullptr),
           "bm_rope_kv_store");
-    // Token t attends to the cache positions up to its own.
-    for (int t = 0; t < T; ++t) {
-      launch_attention(attention_out_ + static_cast<size_t>(t) * dim, q_ + static_cast<size_t>(t) * dim, k_cache,
-                       v_cache, scores_->get(), heads, head_dim, max_seq, pos0 + t + 1);
-    }
+    // All T tokens' attention in one launch: query t over cache positions [0, pos0 + t].
+    check(bm_decode_attention(attention_out_, q_, k_cache, v_cache, nullptr, lens_->get(), pos0 + T, T, heads,
+                              heads, head_dim, max_seq, 1, 0.f, attention_workspace_->get(),
+                              attention_workspace_->size(), BM_F32, nullptr, nullptr),
+          "bm_decode_attention");
     launch_gemm(projected_, attention_out_, w.o_proj, T, dim, dim);
     check(bm_add_rmsnorm(hidden_, projected_, w.ffn_norm, normed_, T, dim, eps, BM_F32, nullptr), "bm_add_rmsnorm");
     launch_gemm(gate_, normed_, w.gate_proj, T, hidden_dim, dim);

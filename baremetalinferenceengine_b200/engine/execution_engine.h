@@ -7,14 +7,14 @@
 // implementation (execution_engine.cu beside it) differs from the reference's
 // run_layers (src/execution_engine.cu:89-128) in two ways:
 //   - all tokens of one forward() call go through each layer together: one
-//     launch per op for the whole batch instead of one per token (attention,
-//     which needs each token's own causal length, still runs per token);
+//     launch per op for the whole batch instead of one per token, attention
+//     included (each token attends to its own causal length in the same launch);
 //   - the memory-bound ops are the fused B200 kernels of bm_layer_ops.h: the
 //     embedding gather, the residual add fused into the RMSNorm that follows it
-//     (:118+:121, :126+:109, :126+:80), and RoPE fused with both KV-cache writes
-//     (:113-115).
-// The GEMM and attention kernels stay the reference's (launch_gemm,
-// launch_attention from its src/kernels.cu): they are outside the layer-op path.
+//     (:118+:121, :126+:109, :126+:80), RoPE fused with both KV-cache writes
+//     (:113-115), and the split decode attention (:116).
+// The GEMMs stay the reference's (launch_gemm from its src/kernels.cu): they are
+// outside the layer-op path.
 #ifndef EXECUTION_ENGINE_H
 #define EXECUTION_ENGINE_H
 
@@ -83,8 +83,9 @@ class ExecutionEngine {
   float* up_ = nullptr;
   float* activated_ = nullptr;
   std::shared_ptr<DeviceBuffer<int>> ids_;
+  std::shared_ptr<DeviceBuffer<int>> lens_;                // attended positions per token
+  std::shared_ptr<DeviceBuffer<char>> attention_workspace_;  // split partials of decode attention
 
-  std::shared_ptr<DeviceBuffer<float>> scores_;  // [num_heads][max_seq]
   std::shared_ptr<DeviceBuffer<float>> logits_;  // [vocab]
   std::shared_ptr<DeviceBuffer<float>> rope_table_;  // [max_seq][head_dim/2] (cos, sin)
 

@@ -302,3 +302,100 @@ def launch_kv_store(cache: torch.Tensor, src: torch.Tensor, seq_pos: int, num_he
     with torch.cuda.device(_dev(src)):
         check(load().bm_kv_store(_ptr(cache), _ptr(src), None, seq_pos, None, 1, num_heads, head_dim, max_seq_len,
                                  1, _lib.BM_F32, None, _stream_arg(stream)))
+
+
+# --------------------------------------------------------------------------
+# Batch-aware KV cache (bm_kv_cache_*)
+# --------------------------------------------------------------------------
+
+class KVCache:
+    """Per-layer K/V caches [num_seqs][kv_heads][max_seq][head_dim] with one length
+    per sequence (the reference's KVCache, include/kv_cache.h:10-40, keeps one
+    position for the whole cache). Create it with the target device current."""
+
+    def __init__(self, num_layers: int, num_seqs: int, num_kv_heads: int, max_seq: int, head_dim: int,
+                 max_tokens: int, dtype: torch.dtype = torch.bfloat16, device=None):
+        self.dtype = dtype
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.shape = (num_seqs, num_kv_heads, max_seq, head_dim)
+        self.num_layers = num_layers
+        handle = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            check(load().bm_kv_cache_create(num_layers, num_seqs, num_kv_heads, max_seq, head_dim, max_tokens,
+                                            _DTYPES[dtype], ctypes.byref(handle)))
+        self._h = handle
+
+    def close(self) -> None:
+        if self._h:
+            with torch.cuda.device(self.device):
+                check(load().bm_kv_cache_destroy(self._h))
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+    def layer_ptrs(self, layer: int):
+        k, v = ctypes.c_void_p(), ctypes.c_void_p()
+        check(load().bm_kv_cache_layer(self._h, layer, ctypes.byref(k), ctypes.byref(v)))
+        return k.value, v.value
+
+    def seq_len(self, seq: int) -> int:
+        n = ctypes.c_int32()
+        check(load().bm_kv_cache_seq_len(self._h, seq, ctypes.byref(n)))
+        return n.value
+
+    def reset(self, seq: int = -1) -> None:
+        check(load().bm_kv_cache_reset(self._h, seq))
+
+    def append(self, seq_ids, stream=None):
+        """Assigns the next position of its sequence to each new token (seq_ids: host
+        ints); returns device pointers (positions, seq_ids) for rope_kv_store."""
+        import numpy as np
+
+        ids = np.ascontiguousarray(np.asarray(seq_ids, dtype=np.int32))
+        pos_p, seq_p = ctypes.c_void_p(), ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            check(load().bm_kv_cache_append(self._h, ids.ctypes.data if ids.size else None, ids.size,
+                                            ctypes.byref(pos_p), ctypes.byref(seq_p),
+                                            _stream(self.device, stream)))
+        return pos_p.value, seq_p.value, ids.size
+
+    def rope_kv_store(self, layer: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, appended,
+                      table: Optional[RopeTable] = None, theta: float = 10000.0,
+                      status: Optional[DeviceStatus] = None, stream=None) -> None:
+        """bm_rope_kv_store into `layer` for the tokens of the last append()."""
+        pos_p, seq_p, rows = appended
+        kc, vc = self.layer_ptrs(layer)
+        num_seqs, hkv, max_seq, hd = self.shape
+        for t, n in ((q, "q"), (k, "k"), (v, "v")):
+            _dense(t, n)
+        _same(q, k, v)
+        if q.dtype != self.dtype or q.shape[0] != rows or k.shape[1] != hkv or q.shape[2] != hd:
+            raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "q/k/v do not match the cache or the appended tokens")
+        with torch.cuda.device(_dev(q)):
+            check(load().bm_rope_kv_store(_ptr(q), _ptr(k), _ptr(v), pos_p, 0, seq_p, kc, vc,
+                                          table.ptr if table else None, table.max_pos if table else 0, theta,
+                                          rows, q.shape[1], hkv, hd, max_seq, num_seqs, bm_dtype(q),
+                                          status.ptr if status else None, _stream(q.device, stream)))
+
+    def views(self, layer: int):
+        """Layer `layer`'s K and V caches as torch tensors viewing the cache's
+        memory (no copy; valid while the cache lives)."""
+        typestr = "<f4" if self.dtype == torch.float32 else "<i2"
+        out = []
+        for p in self.layer_ptrs(layer):
+            arr = _DeviceArray(p, self.shape, typestr)
+            t = torch.as_tensor(arr, device=self.device)
+            out.append(t if self.dtype == torch.float32 else t.view(torch.bfloat16))
+        return out
+
+
+class _DeviceArray:
+    """A raw device allocation described by __cuda_array_interface__ (v3)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}

@@ -184,6 +184,63 @@ int bm_kv_store(void* cache, const void* src, const int32_t* positions,
                 int32_t num_seqs, bm_dtype_t dtype, int32_t* d_status,
                 void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Decode attention: one query token per entry of a batch, GQA.
+ *   out[b][h][:] = softmax_j(q[b][h] . K[s][h/G][j] * scale) . V[s][h/G][j]
+ * over positions j in [0, lens[b]) of cache sequence s = seq_ids[b] (0 when
+ * seq_ids is NULL), G = num_q_heads / num_kv_heads (<= 16), scale <= 0 meaning
+ * 1/sqrt(head_dim). q and out are [batch][num_q_heads][head_dim]; the caches are
+ * [num_seqs][num_kv_heads][max_seq][head_dim] (bm_kv_cache_layer,
+ * bm_rope_kv_store). lens is a device array; max_len is a host-side upper bound
+ * of its entries that sizes the work split. head_dim <= 256 with whole 16-byte
+ * rows. Replaces launch_attention (include/kernels.cuh:41,
+ * src/kernels.cu:225-264: one token, heads = kv heads, three launches).
+ * Long sequences are split across CTAs; the split results need
+ * bm_decode_attention_workspace_size() bytes of device scratch, passed as
+ * `workspace` (caller-owned; its contents need no initialisation). With less
+ * scratch than that (or NULL) each (query, kv head) runs unsplit in one CTA:
+ * same results, less parallelism. A query with an out-of-range sequence or a
+ * length outside [1, max_seq] is skipped and flags *d_status. */
+int bm_decode_attention_workspace_size(int64_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                       int32_t head_dim, int32_t max_len, size_t* bytes_out);
+int bm_decode_attention(void* out, const void* q, const void* k_cache, const void* v_cache,
+                        const int32_t* seq_ids, const int32_t* lens, int32_t max_len, int64_t batch,
+                        int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t max_seq,
+                        int32_t num_seqs, float scale, void* workspace, size_t workspace_bytes,
+                        bm_dtype_t dtype, int32_t* d_status, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Batch-aware static KV cache. Replaces the reference's KVCache
+ * (include/kv_cache.h:10-40, src/kv_cache.cu:4-47), which allocates
+ * [max_batch][kv_heads][max_seq][head_dim] fp32 per layer but keeps one
+ * current_seq_pos_ for the whole cache (src/kv_cache.cu:38-47). Here every
+ * sequence has its own length, and the cache stores fp32 or bf16.
+ *
+ * bm_kv_cache_create allocates, per layer, one K and one V buffer of
+ * num_seqs * num_kv_heads * max_seq * head_dim elements (cudaMalloc, zeroed) on
+ * the current device, plus two int32 device arrays of max_tokens entries for the
+ * positions and sequence ids of one batch. bm_kv_cache_append takes the
+ * sequence id of each of `rows` new tokens (host array), gives each token the
+ * next position of its sequence (tokens of one sequence in the order given),
+ * copies positions and sequence ids to the device arrays on `stream`, and
+ * returns their device pointers for bm_rope_kv_store. It fails, changing
+ * nothing, if a sequence would pass max_seq or rows exceeds max_tokens.
+ * The host copy is synchronous with respect to the host buffer (the call
+ * returns after the upload is queued from the cache's own pinned staging). */
+typedef struct bm_kv_cache bm_kv_cache_t;
+
+int bm_kv_cache_create(int32_t num_layers, int32_t num_seqs, int32_t num_kv_heads, int32_t max_seq,
+                       int32_t head_dim, int32_t max_tokens, bm_dtype_t dtype, bm_kv_cache_t** cache_out);
+int bm_kv_cache_destroy(bm_kv_cache_t* cache);
+/* Device pointers of layer `layer`'s K and V caches, [num_seqs][kv_heads][max_seq][head_dim]. */
+int bm_kv_cache_layer(const bm_kv_cache_t* cache, int32_t layer, void** keys, void** values);
+/* Current length (next position) of sequence `seq`. */
+int bm_kv_cache_seq_len(const bm_kv_cache_t* cache, int32_t seq, int32_t* len_out);
+/* Starts sequence `seq` over (length 0); seq = -1 resets every sequence. */
+int bm_kv_cache_reset(bm_kv_cache_t* cache, int32_t seq);
+int bm_kv_cache_append(bm_kv_cache_t* cache, const int32_t* seq_ids, int64_t rows,
+                       const int32_t** positions_dev, const int32_t** seq_ids_dev, void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

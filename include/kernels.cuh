@@ -36,13 +36,18 @@ void launch_add(float* out, float* a, float* b, int size, cudaStream_t stream = 
 // seq_pos must be in [0, max_seq_len).
 void launch_kv_store(float* cache, float* src, int seq_pos, int num_heads, int head_dim, int max_seq_len, cudaStream_t stream = 0);
 
+// Reference include/kernels.cuh:41. Attention of one query per head over the
+// first seq_len positions of a [num_heads][max_seq_len][head_dim] cache; scores
+// (at least num_heads * seq_len floats) is scratch. Served by the split decode
+// attention of bm_layer_ops.h, which keeps its per-split partials in `scores`.
+void launch_attention(float* out, float* q, float* k_cache, float* v_cache, float* scores, int num_heads, int head_dim, int max_seq_len, int seq_len, cudaStream_t stream = 0);
+
 // Not implemented in this library (outside the layer-op path). An engine built
 // against this header links these from the reference's src/kernels.cu compiled
-// with the five names above renamed away (the recipe is in INTEGRATION.md).
-// Reference include/kernels.cuh:20,23,26,41.
+// with the six names above renamed away (the recipe is in INTEGRATION.md).
+// Reference include/kernels.cuh:20,23,26.
 void launch_gemm(float* C, float* A, float* B, int M, int N, int K, cudaStream_t stream = 0);
 void launch_softmax(float* x, int size, cudaStream_t stream = 0);
 void launch_softmax_batch(float* x, int size, int num_vectors, int stride, cudaStream_t stream = 0);
-void launch_attention(float* out, float* q, float* k_cache, float* v_cache, float* scores, int num_heads, int head_dim, int max_seq_len, int seq_len, cudaStream_t stream = 0);
 
 #endif  // KERNELS_CUH

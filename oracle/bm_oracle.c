@@ -365,3 +365,59 @@ int32_t oracle_layer_step_mt(const OracleStep* s, int64_t r0, int64_t r1, int th
   free(jobs);
   return bad;
 }
+
+/* ------------------------------------------------------------------------- */
+/* Decode attention (tests/kernel_tests.cu:229-258, test_attention):          */
+/*   w[j] = exp(dot(q, k[j]) / sqrt(head_dim)), j < seq_len;                   */
+/*   out[d] = sum_j w[j] / sum(w) * v[j][d],  all in double.                   */
+/* Extended to a batch of queries: query b (num_q_heads heads) attends to      */
+/* sequence seq_ids[b] of the cache [num_seqs][kv_heads][max_seq][head_dim]    */
+/* over positions [0, lens[b]); q head h reads kv head h / (num_q_heads /      */
+/* kv_heads) (GQA). The maximum score is subtracted before exp, which changes  */
+/* nothing in exact arithmetic and keeps exp finite. Returns BAD_* bits; bad   */
+/* queries leave their output untouched.                                        */
+int32_t oracle_decode_attention(void* out, const void* q, const void* k_cache, const void* v_cache,
+                                const int32_t* seq_ids, const int32_t* lens, int64_t batch, int hq, int hkv,
+                                int hd, int max_seq, int num_seqs, int dt) {
+  int32_t bad = 0;
+  const int group = hkv > 0 ? hq / hkv : 1;
+  double* w = (double*)malloc(sizeof(double) * (size_t)(max_seq > 0 ? max_seq : 1));
+  double* acc = (double*)malloc(sizeof(double) * (size_t)hd);
+  for (int64_t b = 0; b < batch; ++b) {
+    const int seq = seq_ids ? seq_ids[b] : 0;
+    const int len = lens[b];
+    if (seq < 0 || seq >= num_seqs) {
+      bad |= BAD_SEQUENCE;
+      continue;
+    }
+    if (len <= 0 || len > max_seq) {
+      bad |= BAD_POSITION;
+      continue;
+    }
+    for (int h = 0; h < hq; ++h) {
+      const int kvh = h / group;
+      const int64_t qoff = (b * hq + h) * (int64_t)hd;
+      const int64_t base = ((int64_t)seq * hkv + kvh) * max_seq * hd;
+      double mx = -INFINITY, total = 0.0;
+      for (int j = 0; j < len; ++j) {
+        double dot = 0.0;
+        for (int d = 0; d < hd; ++d) dot += ld(q, qoff + d, dt) * ld(k_cache, base + (int64_t)j * hd + d, dt);
+        w[j] = dot / sqrt((double)hd);
+        if (w[j] > mx) mx = w[j];
+      }
+      for (int j = 0; j < len; ++j) {
+        w[j] = exp(w[j] - mx);
+        total += w[j];
+      }
+      for (int d = 0; d < hd; ++d) acc[d] = 0.0;
+      for (int j = 0; j < len; ++j) {
+        const double p = w[j] / total;
+        for (int d = 0; d < hd; ++d) acc[d] += p * ld(v_cache, base + (int64_t)j * hd + d, dt);
+      }
+      for (int d = 0; d < hd; ++d) st(out, qoff + d, acc[d], dt);
+    }
+  }
+  free(w);
+  free(acc);
+  return bad;
+}

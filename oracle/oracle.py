@@ -73,6 +73,7 @@ def lib() -> ctypes.CDLL:
                                            cint, cint]),
             "oracle_rope_table": (None, [vp, i32, cint, dbl]),
             "oracle_gather": (i32, [vp, vp, vp, i64, i64, i64, i64, cint]),
+            "oracle_decode_attention": (i32, [vp, vp, vp, vp, vp, vp, i64, cint, cint, cint, cint, cint, cint]),
             "oracle_layer_step": (i32, [ctypes.POINTER(OracleStep), i64, i64]),
             "oracle_layer_step_mt": (i32, [ctypes.POINTER(OracleStep), i64, i64, cint]),
             "oracle_f32_to_bf16": (ctypes.c_uint16, [ctypes.c_float]),

@@ -27,6 +27,7 @@ LEGACY = {
     "launch_swiglu": "_Z13launch_swigluPfS_S_iP11CUstream_st",
     "launch_add": "_Z10launch_addPfS_S_iP11CUstream_st",
     "launch_kv_store": "_Z15launch_kv_storePfS_iiiiP11CUstream_st",
+    "launch_attention": "_Z16launch_attentionPfS_S_S_S_iiiiP11CUstream_st",
 }
 
 
@@ -115,6 +116,15 @@ FAKE = 0x100000  # never dereferenced: every call below fails or returns before 
     lambda L: L.bm_rope_table_fill(FAKE, 8, 7, 1e4, None),                            # odd head_dim
     lambda L: L.bm_rope_table_fill(FAKE, 0, 8, 1e4, None),                            # max_pos 0
     lambda L: L.bm_rope_table_create(8, 8, -1.0, ctypes.byref(ctypes.c_void_p())),     # theta < 0
+    lambda L: L.bm_kv_cache_create(0, 1, 1, 8, 8, 8, 0, ctypes.byref(ctypes.c_void_p())),  # no layers
+    lambda L: L.bm_kv_cache_create(1, 1, 1, 8, 8, 0, 0, ctypes.byref(ctypes.c_void_p())),  # max_tokens 0
+    lambda L: L.bm_kv_cache_create(1, 1, 1, 8, 8, 8, 5, ctypes.byref(ctypes.c_void_p())),  # bad dtype
+    lambda L: L.bm_kv_cache_create(1, 1, 1, 8, 8, 8, 0, None),                        # NULL out
+    lambda L: L.bm_kv_cache_append(None, None, 0, ctypes.byref(ctypes.c_void_p()), ctypes.byref(ctypes.c_void_p()),
+                                   None),                                               # NULL cache
+    lambda L: L.bm_kv_cache_layer(None, 0, ctypes.byref(ctypes.c_void_p()), ctypes.byref(ctypes.c_void_p())),
+    lambda L: L.bm_kv_cache_seq_len(None, 0, ctypes.byref(ctypes.c_int32())),
+    lambda L: L.bm_kv_cache_reset(None, 0),
 ])
 def test_host_checks_reject_before_any_launch(lib, call):
     assert call(lib) == _lib.BM_ERR_INVALID_ARGUMENT
@@ -132,6 +142,7 @@ def test_host_checks_reject_before_any_launch(lib, call):
                                  None, None),
     lambda L: L.bm_kv_store(FAKE, FAKE, None, 0, None, 0, 2, 8, 8, 1, 0, None, None),
     lambda L: L.bm_rope_table_destroy(None),
+    lambda L: L.bm_kv_cache_destroy(None),
 ])
 def test_empty_calls_are_no_ops(lib, call):
     assert call(lib) == _lib.BM_OK

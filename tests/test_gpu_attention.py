@@ -1,0 +1,125 @@
+"""Decode attention (bm_decode_attention) against the oracle on the GPU.
+
+The oracle restates the reference's attention check loop (tests/kernel_tests.cu:
+229-258) in double precision, extended to GQA, batches and per-query lengths.
+fp32 within 1e-5 and bf16 within 1e-2 in the reference's metric.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from baremetalinferenceengine_b200 import _lib, ops
+from oracle import oracle as orc
+from tests.helpers import TOL, bits_equal, gen, randn, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def oracle_attention(q, kc, vc, seq_ids, lens):
+    batch, hq, hd = q.shape
+    num_seqs, hkv, max_seq, _ = kc.shape
+    out = np.zeros_like(to_np(q))
+    bad = orc.lib().oracle_decode_attention(
+        out.ctypes.data, to_np(q).ctypes.data, to_np(kc).ctypes.data, to_np(vc).ctypes.data,
+        None if seq_ids is None else np.ascontiguousarray(seq_ids.numpy()).ctypes.data,
+        np.ascontiguousarray(lens.numpy()).ctypes.data, batch, hq, hkv, hd, max_seq, num_seqs,
+        0 if q.dtype == torch.float32 else 1)
+    return out, bad
+
+
+def run(cuda, q, kc, vc, seq_ids, lens, workspace=True, status=None):
+    batch, hq, hd = q.shape
+    num_seqs, hkv, max_seq, _ = kc.shape
+    L = _lib.load()
+    max_len = int(lens.max()) if lens.numel() else 1
+    need = ctypes.c_size_t()
+    _lib.check(L.bm_decode_attention_workspace_size(batch, hq, hkv, hd, max_len, ctypes.byref(need)))
+    ws = torch.empty(max(need.value, 1), dtype=torch.uint8, device=cuda) if workspace else None
+    out = torch.full((batch, hq, hd), 7.0, dtype=q.dtype, device=cuda)
+    qd, kd, vd = q.to(cuda), kc.to(cuda), vc.to(cuda)
+    sd = None if seq_ids is None else seq_ids.to(cuda)
+    ld = lens.to(cuda)
+    _lib.check(L.bm_decode_attention(out.data_ptr(), qd.data_ptr(), kd.data_ptr(), vd.data_ptr(),
+                                     None if sd is None else sd.data_ptr(), ld.data_ptr(), max_len, batch, hq, hkv,
+                                     hd, max_seq, num_seqs, 0.0, None if ws is None else ws.data_ptr(),
+                                     need.value if ws is not None else 0, ops.bm_dtype(q),
+                                     None if status is None else status.ptr,
+                                     torch.cuda.current_stream(cuda).cuda_stream))
+    return out, need.value
+
+
+ORACLE_DT = [torch.float32, torch.bfloat16]
+
+
+@pytest.mark.parametrize("dt", ORACLE_DT, ids=["f32", "bf16"])
+@pytest.mark.parametrize("batch,hq,hkv,hd,max_seq,num_seqs", [
+    (1, 6, 6, 48, 256, 1),        # tinyllama: the reference's own shape (heads = kv heads)
+    (16, 32, 8, 128, 8192, 16),   # Llama-3-8B decode, GQA group 4
+    (4, 64, 8, 128, 8192, 4),     # Llama-3-70B decode, GQA group 8
+    (3, 32, 2, 64, 1024, 5),      # group 16, head_dim 64
+    (2, 4, 4, 256, 600, 2),       # head_dim 256
+])
+@pytest.mark.parametrize("workspace", [True, False], ids=["split", "unsplit"])
+def test_decode_attention_matches_oracle(cuda, dt, batch, hq, hkv, hd, max_seq, num_seqs, workspace):
+    g = gen(batch * 1000 + hq + hd)
+    q = randn((batch, hq, hd), dt, g)
+    kc = randn((num_seqs, hkv, max_seq, hd), dt, g)
+    vc = randn((num_seqs, hkv, max_seq, hd), dt, g)
+    seq_ids = torch.randint(0, num_seqs, (batch,), generator=g, dtype=torch.int32)
+    lens = torch.randint(1, max_seq + 1, (batch,), generator=g, dtype=torch.int32)
+    lens[0] = max_seq  # the full cache
+    if batch > 1:
+        lens[1] = 1  # a single position
+    out, need = run(cuda, q, kc, vc, seq_ids, lens, workspace)
+    want, bad = oracle_attention(q, kc, vc, seq_ids, lens)
+    assert bad == 0
+    assert orc.worst_error(to_np(out), want) <= TOL[dt]
+
+
+def test_reference_attention_cases(cuda):
+    """The reference's three attention checks (tests/kernel_tests.cu:285-287):
+    inputs U[-1,1], one query, heads = kv heads."""
+    for heads, hd, max_seq, seq_len in [(1, 16, 1, 1), (6, 48, 256, 1), (6, 48, 256, 200)]:
+        g = gen(heads + seq_len)
+        q = torch.rand(1, heads, hd, generator=g) * 2 - 1
+        kc = torch.rand(1, heads, max_seq, hd, generator=g) * 2 - 1
+        vc = torch.rand(1, heads, max_seq, hd, generator=g) * 2 - 1
+        lens = torch.tensor([seq_len], dtype=torch.int32)
+        out, _ = run(cuda, q, kc, vc, None, lens)
+        want, _ = oracle_attention(q, kc, vc, None, lens)
+        assert orc.worst_error(to_np(out), want) <= 1e-5
+
+
+def test_bad_entries_are_skipped_and_flagged(cuda):
+    g = gen(9)
+    q = torch.randn(4, 8, 64, generator=g)
+    kc, vc = torch.randn(2, 2, 32, 64, generator=g), torch.randn(2, 2, 32, 64, generator=g)
+    seq_ids = torch.tensor([0, 2, 1, -1], dtype=torch.int32)
+    lens = torch.tensor([5, 5, 0, 3], dtype=torch.int32)
+    status = ops.DeviceStatus(cuda)
+    out, _ = run(cuda, q, kc, vc, seq_ids, lens, status=status)
+    assert status.read() == _lib.BM_DEVERR_BAD_SEQUENCE | _lib.BM_DEVERR_BAD_POSITION
+    want, bad = oracle_attention(q, kc, vc, seq_ids, lens)
+    assert bad == _lib.BM_DEVERR_BAD_SEQUENCE | _lib.BM_DEVERR_BAD_POSITION
+    outc = out.cpu()
+    assert orc.worst_error(outc[0].numpy(), want[0]) <= 1e-5
+    for b in (1, 2, 3):
+        assert bits_equal(outc[b], torch.full((8, 64), 7.0))
+
+
+def test_workspace_size_and_argument_checks(cuda):
+    L = _lib.load()
+    n = ctypes.c_size_t()
+    _lib.check(L.bm_decode_attention_workspace_size(1, 8, 8, 128, 8192, ctypes.byref(n)))
+    assert n.value > 0  # one long query is split across CTAs
+    _lib.check(L.bm_decode_attention_workspace_size(1, 8, 8, 128, 100, ctypes.byref(n)))
+    assert n.value == 0  # a single tile needs no split
+    dummy = torch.zeros(64, device=cuda)
+    p = dummy.data_ptr()
+    lens = torch.ones(1, dtype=torch.int32, device=cuda)
+    for args in [(1, 6, 4, 64), (1, 32, 1, 64), (1, 8, 8, 300), (1, 8, 8, 34)]:
+        st = L.bm_decode_attention(p, p, p, p, None, lens.data_ptr(), 1, args[0], args[1], args[2], args[3], 8, 1,
+                                   0.0, None, 0, 0, None, None)
+        assert st == _lib.BM_ERR_INVALID_ARGUMENT, args
