@@ -15,8 +15,9 @@
 //           shared memory;
 //   softmax: running max and sum per query, base-2 exponentials (exp2f), tile
 //           maxima and sums by warp shuffles plus a shared-memory pass;
-//   mix:    warp w takes positions w, w+4, ...; lane l owns dimensions
-//           l, l+32, ... and accumulates p * V for the G queries.
+//   mix:    warp w takes positions w, w+4, ...; lane l owns head_dim/32
+//           dimensions (contiguous, one vector load, when head_dim is a
+//           multiple of 32) and accumulates p * V for the G queries.
 // The four warps' accumulators are summed through shared memory at the end.
 // With one split the CTA writes the normalised output; with several it writes
 // (max, sum, unnormalised output) per query to the workspace and
@@ -93,11 +94,45 @@ __device__ __forceinline__ void block_reduce(float (&vals)[GM], int G, float (*s
   __syncthreads();
 }
 
+// Loads N consecutive elements of T (N * sizeof(T) in {2, 4, 8, 16} bytes, aligned) as floats.
+template <typename T, int N>
+__device__ __forceinline__ void load_n(const T* p, float* f) {
+  constexpr int kBytes = N * static_cast<int>(sizeof(T));
+  if constexpr (kBytes == 16) {
+    unpack16<T>(__ldg(reinterpret_cast<const uint4*>(p)), f);
+  } else if constexpr (kBytes == 8) {
+    const uint2 r = __ldg(reinterpret_cast<const uint2*>(p));
+    if constexpr (sizeof(T) == 4) {
+      f[0] = __uint_as_float(r.x);
+      f[1] = __uint_as_float(r.y);
+    } else {
+      f[0] = bf16_lo(r.x);
+      f[1] = bf16_hi(r.x);
+      f[2] = bf16_lo(r.y);
+      f[3] = bf16_hi(r.y);
+    }
+  } else if constexpr (kBytes == 4) {
+    const uint32_t r = __ldg(reinterpret_cast<const unsigned int*>(p));
+    if constexpr (sizeof(T) == 4) {
+      f[0] = __uint_as_float(r);
+    } else {
+      f[0] = bf16_lo(r);
+      f[1] = bf16_hi(r);
+    }
+  } else {
+    f[0] = load1<T>(p);
+  }
+}
+
 // GM: the group size rounded up to a power of two (register arrays are sized by
-// it); DPL = ceil(head_dim / 32): lane l owns dimensions l, l + 32, ... of the mix.
-template <typename T, int GM, int DPL>
+// it); DPL = ceil(head_dim / 32) dimensions per lane in the mix. CONTIG (head_dim
+// = 32 * DPL, DPL a power of two): lane l owns dimensions [l*DPL, l*DPL + DPL)
+// and reads them with one vector load; otherwise it owns l, l + 32, ...
+template <typename T, int GM, int DPL, bool CONTIG>
 __global__ void __launch_bounds__(kThreads) attention_split_kernel(AttnArgs a) {
   constexpr int VEC = VecWidth<T>::value;
+  constexpr int KCHUNKS = (32 * DPL + VEC - 1) / VEC;  // 16-byte chunks of the longest K row
+  constexpr int KB = KCHUNKS < 8 ? KCHUNKS : 8;           // chunks loaded together
   extern __shared__ float smem[];
   // layout: q_s [G][hd] | p_s [G][kThreads] | red [kWarps][G][hd]
   const int G = a.group, hd = a.hd;
@@ -138,6 +173,7 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(AttnArgs a) {
   const int64_t head_base = (static_cast<int64_t>(seq) * a.hkv + kvh) * a.max_seq * hd;
   const T* kbase = static_cast<const T*>(a.k_cache) + head_base;
   const T* vbase = static_cast<const T*>(a.v_cache) + head_base;
+  auto dim_of = [&](int i) { return CONTIG ? lane * DPL + i : lane + 32 * i; };
 
   float acc[GM][DPL];
 #pragma unroll
@@ -152,17 +188,30 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(AttnArgs a) {
 #pragma unroll
     for (int g = 0; g < GM; ++g) s[g] = 0.f;
     if (p < end) {
+      // the K row in batches of KB 16-byte chunks (compile-time counts), each
+      // batch's loads in flight together
       const T* krow = kbase + static_cast<int64_t>(p) * hd;
-      for (int c = 0; c < hd; c += VEC) {
-        float k[VEC];
-        unpack16<T>(__ldg(reinterpret_cast<const uint4*>(krow + c)), k);
 #pragma unroll
-        for (int g = 0; g < GM; ++g) {
-          if (g < G) {
-            float dot = s[g];
+      for (int cb = 0; cb < KCHUNKS; cb += KB) {
+        uint4 kr[KB];
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) dot = fmaf(q_s[g * hd + c + e], k[e], dot);
-            s[g] = dot;
+        for (int c = 0; c < KB; ++c) {
+          if ((cb + c) * VEC < hd) kr[c] = __ldg(reinterpret_cast<const uint4*>(krow + (cb + c) * VEC));
+        }
+#pragma unroll
+        for (int c = 0; c < KB; ++c) {
+          if ((cb + c) * VEC < hd) {
+            float k[VEC];
+            unpack16<T>(kr[c], k);
+#pragma unroll
+            for (int g = 0; g < GM; ++g) {
+              if (g < G) {
+                float dot = s[g];
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) dot = fmaf(q_s[g * hd + (cb + c) * VEC + e], k[e], dot);
+                s[g] = dot;
+              }
+            }
           }
         }
       }
@@ -201,7 +250,8 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(AttnArgs a) {
       m_s[tid] = m_mine;
     }
     __syncthreads();
-    // mix: rescale, then accumulate p * V over this warp's positions of the tile
+    // mix: rescale, then accumulate p * V over this warp's positions of the tile,
+    // two positions' V loads in flight at a time
 #pragma unroll
     for (int g = 0; g < GM; ++g) {
       if (g < G) {
@@ -211,20 +261,34 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(AttnArgs a) {
       }
     }
     const int tile_end = min(end - tile, kThreads);
-    for (int j = warp; j < tile_end; j += kWarps) {
-      const T* vrow = vbase + static_cast<int64_t>(tile + j) * hd;
-      float v[DPL];
+    for (int j0 = warp; j0 < tile_end; j0 += 2 * kWarps) {
+      float v[2][DPL];
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) {
-        const int d = lane + 32 * i;
-        v[i] = d < hd ? load1<T>(vrow + d) : 0.f;
+      for (int u = 0; u < 2; ++u) {
+        const int j = j0 + u * kWarps;
+        const T* vrow = vbase + static_cast<int64_t>(tile + min(j, tile_end - 1)) * hd;
+        if constexpr (CONTIG) {
+          load_n<T, DPL>(vrow + lane * DPL, v[u]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) {
+            const int d = lane + 32 * i;
+            v[u][i] = d < hd ? load1<T>(vrow + d) : 0.f;
+          }
+        }
       }
 #pragma unroll
-      for (int g = 0; g < GM; ++g) {
-        if (g < G) {
-          const float pr = p_s[g * kThreads + j];
+      for (int u = 0; u < 2; ++u) {
+        const int j = j0 + u * kWarps;
+        if (j < tile_end) {
 #pragma unroll
-          for (int i = 0; i < DPL; ++i) acc[g][i] = fmaf(pr, v[i], acc[g][i]);
+          for (int g = 0; g < GM; ++g) {
+            if (g < G) {
+              const float pr = p_s[g * kThreads + j];
+#pragma unroll
+              for (int i = 0; i < DPL; ++i) acc[g][i] = fmaf(pr, v[u][i], acc[g][i]);
+            }
+          }
         }
       }
     }
@@ -237,7 +301,7 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(AttnArgs a) {
     if (g < G) {
 #pragma unroll
       for (int i = 0; i < DPL; ++i) {
-        const int d = lane + 32 * i;
+        const int d = dim_of(i);
         if (d < hd) red[(warp * G + g) * hd + d] = acc[g][i];
       }
     }
@@ -333,15 +397,16 @@ int launch_group(const AttnArgs& a, size_t smem, cudaStream_t stream) {
     kernel<<<grid, kThreads, smem, stream>>>(a);
     return check_launch("bm_decode_attention");
   };
+  const bool contig = a.hd % 32 == 0;
   switch ((a.hd + 31) / 32) {
-    case 1: return go(attention_split_kernel<T, GM, 1>);
-    case 2: return go(attention_split_kernel<T, GM, 2>);
-    case 3: return go(attention_split_kernel<T, GM, 3>);
-    case 4: return go(attention_split_kernel<T, GM, 4>);
-    case 5: return go(attention_split_kernel<T, GM, 5>);
-    case 6: return go(attention_split_kernel<T, GM, 6>);
-    case 7: return go(attention_split_kernel<T, GM, 7>);
-    default: return go(attention_split_kernel<T, GM, 8>);
+    case 1: return contig ? go(attention_split_kernel<T, GM, 1, true>) : go(attention_split_kernel<T, GM, 1, false>);
+    case 2: return contig ? go(attention_split_kernel<T, GM, 2, true>) : go(attention_split_kernel<T, GM, 2, false>);
+    case 3: return go(attention_split_kernel<T, GM, 3, false>);
+    case 4: return contig ? go(attention_split_kernel<T, GM, 4, true>) : go(attention_split_kernel<T, GM, 4, false>);
+    case 5: return go(attention_split_kernel<T, GM, 5, false>);
+    case 6: return go(attention_split_kernel<T, GM, 6, false>);
+    case 7: return go(attention_split_kernel<T, GM, 7, false>);
+    default: return contig ? go(attention_split_kernel<T, GM, 8, true>) : go(attention_split_kernel<T, GM, 8, false>);
   }
 }
 

@@ -126,11 +126,13 @@ def to_f64(a: np.ndarray) -> np.ndarray:
 
 def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float = 1e-5) -> np.ndarray:
     """oracle_rmsnorm (tests/kernel_tests.cu:75-79) over the rows of x [rows, dim]."""
-    x = _c(x)
+    # Every array a C call reads is bound to a name first: a temporary copy's
+    # memory could be freed before the call runs.
+    x, w = _c(x), _c(w)
     out = np.empty_like(x)
     dim = x.shape[-1]
     rows = x.size // dim if dim else 0
-    lib().oracle_rmsnorm(_p(out), _p(x), _p(_c(w)), rows, dim, eps, dim, dim, _dt(x))
+    lib().oracle_rmsnorm(_p(out), _p(x), _p(w), rows, dim, eps, dim, dim, _dt(x))
     return out
 
 
@@ -145,9 +147,10 @@ def add(a: np.ndarray, b: np.ndarray) -> np.ndarray:
 def add_rmsnorm(h: np.ndarray, p: np.ndarray, w: np.ndarray, eps: float = 1e-5):
     """Returns (h + p, rmsnorm(h + p) * w): oracle_add_rmsnorm."""
     h2 = np.array(h, copy=True, order="C")
+    p, w = _c(p), _c(w)
     y = np.empty_like(h2)
     dim = h2.shape[-1]
-    lib().oracle_add_rmsnorm(_p(h2), _p(_c(p)), _p(_c(w)), _p(y), h2.size // dim, dim, eps, _dt(h2))
+    lib().oracle_add_rmsnorm(_p(h2), _p(p), _p(w), _p(y), h2.size // dim, dim, eps, _dt(h2))
     return h2, y
 
 
@@ -178,7 +181,8 @@ def kv_store(cache: np.ndarray, src: np.ndarray, positions, seq_ids=None):
     pos_arr = None if isinstance(positions, (int, np.integer)) else np.ascontiguousarray(positions, np.int32)
     pos0 = int(positions) if pos_arr is None else 0
     seq = None if seq_ids is None else np.ascontiguousarray(seq_ids, np.int32)
-    bad = lib().oracle_kv_store(_p(c), _p(_c(src)), _p(pos_arr), pos0, _p(seq), rows, heads, hd, c.shape[2],
+    src = _c(src)
+    bad = lib().oracle_kv_store(_p(c), _p(src), _p(pos_arr), pos0, _p(seq), rows, heads, hd, c.shape[2],
                                 c.shape[0], _dt(c))
     return c, bad
 
@@ -193,7 +197,8 @@ def rope_kv_store(q, k, v, positions, k_cache, v_cache, theta, seq_ids=None, tab
     pos_arr = None if isinstance(positions, (int, np.integer)) else np.ascontiguousarray(positions, np.int32)
     pos0 = int(positions) if pos_arr is None else 0
     seq = None if seq_ids is None else np.ascontiguousarray(seq_ids, np.int32)
-    bad = lib().oracle_rope_kv_store(_p(q2), _p(_c(k)), _p(_c(v)), _p(pos_arr), pos0, _p(seq), _p(kc), _p(vc),
+    k, v = _c(k), _c(v)
+    bad = lib().oracle_rope_kv_store(_p(q2), _p(k), _p(v), _p(pos_arr), pos0, _p(seq), _p(kc), _p(vc),
                                      table_len, theta, rows, hq, hkv, hd, kc.shape[2], kc.shape[0], _dt(q2))
     return q2, kc, vc, bad
 

@@ -20,12 +20,15 @@ pytestmark = pytest.mark.gpu
 def oracle_attention(q, kc, vc, seq_ids, lens):
     batch, hq, hd = q.shape
     num_seqs, hkv, max_seq, _ = kc.shape
-    out = np.zeros_like(to_np(q))
+    # every array the C call reads is bound to a name: a temporary's memory could be
+    # freed before the call runs
+    qn, kn, vn = to_np(q), to_np(kc), to_np(vc)
+    sn = None if seq_ids is None else np.ascontiguousarray(seq_ids.numpy(), dtype=np.int32)
+    ln = np.ascontiguousarray(lens.numpy(), dtype=np.int32)
+    out = np.zeros_like(qn)
     bad = orc.lib().oracle_decode_attention(
-        out.ctypes.data, to_np(q).ctypes.data, to_np(kc).ctypes.data, to_np(vc).ctypes.data,
-        None if seq_ids is None else np.ascontiguousarray(seq_ids.numpy()).ctypes.data,
-        np.ascontiguousarray(lens.numpy()).ctypes.data, batch, hq, hkv, hd, max_seq, num_seqs,
-        0 if q.dtype == torch.float32 else 1)
+        out.ctypes.data, qn.ctypes.data, kn.ctypes.data, vn.ctypes.data, None if sn is None else sn.ctypes.data,
+        ln.ctypes.data, batch, hq, hkv, hd, max_seq, num_seqs, 0 if q.dtype == torch.float32 else 1)
     return out, bad
 
 
