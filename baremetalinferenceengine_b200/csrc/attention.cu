@@ -22,340 +22,11 @@
 // With one split the CTA writes the normalised output; with several it writes
 // (max, sum, unnormalised output) per query to the workspace and
 // attention_combine_kernel merges the splits.
-#include <algorithm>
-#include <cmath>
-
-#include "bm_common.cuh"
-#include "bm_host.h"
+#include "attention_kernels.cuh"
 
 namespace bm {
-namespace {
+namespace attn {
 
-constexpr int kThreads = 128;  // = positions per tile
-constexpr int kWarps = kThreads / 32;
-constexpr int kMaxGroup = 16;
-constexpr int kMaxHeadDim = 256;
-
-struct AttnArgs {
-  void* out;              // [batch][hq][hd]
-  const void* q;          // [batch][hq][hd]
-  const void* k_cache;    // [num_seqs][hkv][max_seq][hd]
-  const void* v_cache;
-  const int32_t* seq_ids; // NULL: 0
-  const int32_t* lens;    // NULL: len0 for every query
-  int32_t len0;
-  int64_t batch;
-  int hq, hkv, hd, group, max_seq, num_seqs;
-  int splits, split_len;  // positions per split (a multiple of kThreads)
-  float qscale;           // log2(e) * softmax scale
-  float* ws;              // [batch][hkv][splits][group][hd + 2]: o..., m, l
-  int32_t* status;
-};
-
-__device__ __forceinline__ int query_len(const AttnArgs& a, int64_t b) { return a.lens ? a.lens[b] : a.len0; }
-
-// Returns the query's status bits (0 = valid).
-__device__ __forceinline__ int32_t check_query(const AttnArgs& a, int64_t b, int* seq, int* len) {
-  *seq = a.seq_ids ? a.seq_ids[b] : 0;
-  *len = query_len(a, b);
-  int32_t bad = 0;
-  if (*seq < 0 || *seq >= a.num_seqs) bad |= BM_DEVERR_BAD_SEQUENCE;
-  if (*len <= 0 || *len > a.max_seq) bad |= BM_DEVERR_BAD_POSITION;
-  return bad;
-}
-
-// Block-wide max or sum of G values per thread (vals[g]); every thread gets the results.
-// (Loops run to the compile-time GM so the register array is never indexed at run time.)
-template <bool MAX, int GM>
-__device__ __forceinline__ void block_reduce(float (&vals)[GM], int G, float (*scratch)[kMaxGroup]) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-  for (int g = 0; g < GM; ++g) {
-    if (g < G) {
-      float v = vals[g];
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        const float o = __shfl_xor_sync(0xffffffffu, v, off);
-        v = MAX ? fmaxf(v, o) : v + o;
-      }
-      if (lane == 0) scratch[warp][g] = v;
-    }
-  }
-  __syncthreads();
-#pragma unroll
-  for (int g = 0; g < GM; ++g) {
-    if (g < G) {
-      float v = scratch[0][g];
-#pragma unroll
-      for (int w = 1; w < kWarps; ++w) v = MAX ? fmaxf(v, scratch[w][g]) : v + scratch[w][g];
-      vals[g] = v;
-    }
-  }
-  __syncthreads();
-}
-
-// Loads N consecutive elements of T (N * sizeof(T) in {2, 4, 8, 16} bytes, aligned) as floats.
-template <typename T, int N>
-__device__ __forceinline__ void load_n(const T* p, float* f) {
-  constexpr int kBytes = N * static_cast<int>(sizeof(T));
-  if constexpr (kBytes == 16) {
-    unpack16<T>(__ldg(reinterpret_cast<const uint4*>(p)), f);
-  } else if constexpr (kBytes == 8) {
-    const uint2 r = __ldg(reinterpret_cast<const uint2*>(p));
-    if constexpr (sizeof(T) == 4) {
-      f[0] = __uint_as_float(r.x);
-      f[1] = __uint_as_float(r.y);
-    } else {
-      f[0] = bf16_lo(r.x);
-      f[1] = bf16_hi(r.x);
-      f[2] = bf16_lo(r.y);
-      f[3] = bf16_hi(r.y);
-    }
-  } else if constexpr (kBytes == 4) {
-    const uint32_t r = __ldg(reinterpret_cast<const unsigned int*>(p));
-    if constexpr (sizeof(T) == 4) {
-      f[0] = __uint_as_float(r);
-    } else {
-      f[0] = bf16_lo(r);
-      f[1] = bf16_hi(r);
-    }
-  } else {
-    f[0] = load1<T>(p);
-  }
-}
-
-// GM: the group size rounded up to a power of two (register arrays are sized by
-// it); DPL = ceil(head_dim / 32) dimensions per lane in the mix. CONTIG (head_dim
-// = 32 * DPL, DPL a power of two): lane l owns dimensions [l*DPL, l*DPL + DPL)
-// and reads them with one vector load; otherwise it owns l, l + 32, ...
-template <typename T, int GM, int DPL, bool CONTIG>
-__global__ void __launch_bounds__(kThreads) attention_split_kernel(AttnArgs a) {
-  constexpr int VEC = VecWidth<T>::value;
-  constexpr int KCHUNKS = (32 * DPL + VEC - 1) / VEC;  // 16-byte chunks of the longest K row
-  constexpr int KB = KCHUNKS < 8 ? KCHUNKS : 8;           // chunks loaded together
-  extern __shared__ float smem[];
-  // layout: q_s [G][hd] | p_s [G][kThreads] | red [kWarps][G][hd]
-  const int G = a.group, hd = a.hd;
-  float* q_s = smem;
-  float* p_s = q_s + G * hd;
-  float* red = p_s + G * kThreads;
-  __shared__ float scratch[kWarps][kMaxGroup];
-  __shared__ float m_s[kMaxGroup], l_s[kMaxGroup], alpha_s[kMaxGroup];
-
-  const int64_t b = blockIdx.z;
-  const int kvh = blockIdx.y;
-  const int split = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  int seq, len;
-  const int32_t bad = check_query(a, b, &seq, &len);
-  if (bad) {  // uniform: every thread of the CTA read the same query
-    if (tid == 0 && kvh == 0 && split == 0) raise_status(a.status, bad);
-    return;
-  }
-  const int start = split * a.split_len;
-  const int end = min(len, start + a.split_len);
-  float* ws = a.ws ? a.ws + (((b * a.hkv + kvh) * a.splits + split) * G) * static_cast<int64_t>(hd + 2) : nullptr;
-  if (start >= end) {  // this split lies past the query's length: an empty partial
-    if (ws != nullptr && tid < G) {
-      ws[tid * (hd + 2) + hd] = -INFINITY;
-      ws[tid * (hd + 2) + hd + 1] = 0.f;
-    }
-    return;
-  }
-
-  // queries of the group, pre-scaled, in shared memory
-  const T* qb = static_cast<const T*>(a.q) + (b * a.hq + static_cast<int64_t>(kvh) * G) * hd;
-  for (int i = tid; i < G * hd; i += kThreads) q_s[i] = load1<T>(qb + i) * a.qscale;
-  if (tid < G) {
-    m_s[tid] = -INFINITY;
-    l_s[tid] = 0.f;
-  }
-  const int64_t head_base = (static_cast<int64_t>(seq) * a.hkv + kvh) * a.max_seq * hd;
-  const T* kbase = static_cast<const T*>(a.k_cache) + head_base;
-  const T* vbase = static_cast<const T*>(a.v_cache) + head_base;
-  auto dim_of = [&](int i) { return CONTIG ? lane * DPL + i : lane + 32 * i; };
-
-  float acc[GM][DPL];
-#pragma unroll
-  for (int g = 0; g < GM; ++g)
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) acc[g][i] = 0.f;
-  __syncthreads();
-
-  for (int tile = start; tile < end; tile += kThreads) {
-    const int p = tile + tid;
-    float s[GM];
-#pragma unroll
-    for (int g = 0; g < GM; ++g) s[g] = 0.f;
-    if (p < end) {
-      // the K row in batches of KB 16-byte chunks (compile-time counts), each
-      // batch's loads in flight together
-      const T* krow = kbase + static_cast<int64_t>(p) * hd;
-#pragma unroll
-      for (int cb = 0; cb < KCHUNKS; cb += KB) {
-        uint4 kr[KB];
-#pragma unroll
-        for (int c = 0; c < KB; ++c) {
-          if ((cb + c) * VEC < hd) kr[c] = __ldg(reinterpret_cast<const uint4*>(krow + (cb + c) * VEC));
-        }
-#pragma unroll
-        for (int c = 0; c < KB; ++c) {
-          if ((cb + c) * VEC < hd) {
-            float k[VEC];
-            unpack16<T>(kr[c], k);
-#pragma unroll
-            for (int g = 0; g < GM; ++g) {
-              if (g < G) {
-                float dot = s[g];
-#pragma unroll
-                for (int e = 0; e < VEC; ++e) dot = fmaf(q_s[g * hd + (cb + c) * VEC + e], k[e], dot);
-                s[g] = dot;
-              }
-            }
-          }
-        }
-      }
-    } else {
-#pragma unroll
-      for (int g = 0; g < GM; ++g) s[g] = -INFINITY;
-    }
-    // online softmax (base 2): tile max, rescale factors, probabilities, tile sum
-    float t[GM];
-#pragma unroll
-    for (int g = 0; g < GM; ++g) t[g] = s[g];
-    block_reduce<true, GM>(t, G, scratch);
-#pragma unroll
-    for (int g = 0; g < GM; ++g) {
-      if (g < G) {
-        const float m_new = fmaxf(m_s[g], t[g]);
-        const float pr = (p < end) ? exp2f(s[g] - m_new) : 0.f;
-        p_s[g * kThreads + tid] = pr;
-        t[g] = pr;
-        s[g] = m_new;  // reuse: the new running max
-      }
-    }
-    block_reduce<false, GM>(t, G, scratch);  // tile sums; its barriers also publish p_s
-    float m_mine = 0.f, sum_mine = 0.f;  // thread g < G updates query g's running state
-#pragma unroll
-    for (int g = 0; g < GM; ++g) {
-      if (g == tid) {
-        m_mine = s[g];
-        sum_mine = t[g];
-      }
-    }
-    if (tid < G) {
-      const float alpha = exp2f(m_s[tid] - m_mine);
-      alpha_s[tid] = alpha;
-      l_s[tid] = l_s[tid] * alpha + sum_mine;
-      m_s[tid] = m_mine;
-    }
-    __syncthreads();
-    // mix: rescale, then accumulate p * V over this warp's positions of the tile,
-    // two positions' V loads in flight at a time
-#pragma unroll
-    for (int g = 0; g < GM; ++g) {
-      if (g < G) {
-        const float al = alpha_s[g];
-#pragma unroll
-        for (int i = 0; i < DPL; ++i) acc[g][i] *= al;
-      }
-    }
-    const int tile_end = min(end - tile, kThreads);
-    for (int j0 = warp; j0 < tile_end; j0 += 2 * kWarps) {
-      float v[2][DPL];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int j = j0 + u * kWarps;
-        const T* vrow = vbase + static_cast<int64_t>(tile + min(j, tile_end - 1)) * hd;
-        if constexpr (CONTIG) {
-          load_n<T, DPL>(vrow + lane * DPL, v[u]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < DPL; ++i) {
-            const int d = lane + 32 * i;
-            v[u][i] = d < hd ? load1<T>(vrow + d) : 0.f;
-          }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int j = j0 + u * kWarps;
-        if (j < tile_end) {
-#pragma unroll
-          for (int g = 0; g < GM; ++g) {
-            if (g < G) {
-              const float pr = p_s[g * kThreads + j];
-#pragma unroll
-              for (int i = 0; i < DPL; ++i) acc[g][i] = fmaf(pr, v[u][i], acc[g][i]);
-            }
-          }
-        }
-      }
-    }
-    __syncthreads();  // p_s, alpha_s are rewritten by the next tile
-  }
-
-  // sum the warps' accumulators
-#pragma unroll
-  for (int g = 0; g < GM; ++g) {
-    if (g < G) {
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) {
-        const int d = dim_of(i);
-        if (d < hd) red[(warp * G + g) * hd + d] = acc[g][i];
-      }
-    }
-  }
-  __syncthreads();
-  for (int i = tid; i < G * hd; i += kThreads) {
-    float o = red[i];
-#pragma unroll
-    for (int w = 1; w < kWarps; ++w) o += red[w * G * hd + i];
-    const int g = i / hd, d = i - g * hd;
-    if (ws == nullptr) {
-      T* out = static_cast<T*>(a.out) + (b * a.hq + static_cast<int64_t>(kvh) * G + g) * hd;
-      store1<T>(out + d, o / l_s[g]);
-    } else {
-      ws[g * (hd + 2) + d] = o;
-      if (d == 0) {
-        ws[g * (hd + 2) + hd] = m_s[g];
-        ws[g * (hd + 2) + hd + 1] = l_s[g];
-      }
-    }
-  }
-}
-
-// One CTA per (query, q head): merges the splits' (max, sum, output) partials.
-template <typename T>
-__global__ void __launch_bounds__(256) attention_combine_kernel(AttnArgs a) {
-  const int64_t b = blockIdx.y;
-  const int h = blockIdx.x;
-  int seq, len;
-  if (check_query(a, b, &seq, &len)) return;  // reported by the split kernel
-  const int kvh = h / a.group, g = h - kvh * a.group;
-  const int hd = a.hd;
-  const float* base = a.ws + ((b * a.hkv + kvh) * a.splits * a.group + g) * static_cast<int64_t>(hd + 2);
-  const int64_t split_stride = static_cast<int64_t>(a.group) * (hd + 2);
-  float m = -INFINITY;
-  for (int s = 0; s < a.splits; ++s) m = fmaxf(m, base[s * split_stride + hd]);
-  float l = 0.f;
-  for (int s = 0; s < a.splits; ++s) {
-    const float ms = base[s * split_stride + hd];
-    if (ms != -INFINITY) l += base[s * split_stride + hd + 1] * exp2f(ms - m);
-  }
-  T* out = static_cast<T*>(a.out) + (b * a.hq + h) * hd;
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    float o = 0.f;
-    for (int s = 0; s < a.splits; ++s) {
-      const float ms = base[s * split_stride + hd];
-      if (ms != -INFINITY) o += base[s * split_stride + d] * exp2f(ms - m);
-    }
-    store1<T>(out + d, o / l);
-  }
-}
-
-// Splits for `pairs` (query, kv head) pairs over at most max_len positions:
-// enough CTAs to fill the GPU several times, each split a whole number of tiles.
 void plan_splits(int64_t pairs, int max_len, int sms, int* splits, int* split_len) {
   const int tiles = (max_len + kThreads - 1) / kThreads;
   const int64_t want = std::max<int64_t>(1, (static_cast<int64_t>(sms) * 4 + pairs - 1) / pairs);
@@ -386,52 +57,11 @@ int check_args(const char* what, int64_t batch, int hq, int hkv, int hd, int max
   return BM_OK;
 }
 
-template <typename T, int GM>
-int launch_group(const AttnArgs& a, size_t smem, cudaStream_t stream) {
-  const dim3 grid(a.splits, a.hkv, static_cast<unsigned>(a.batch));
-  auto go = [&](auto kernel) {
-    if (smem > 48 * 1024) {
-      cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-      if (err != cudaSuccess) return fail(BM_ERR_CUDA, "bm_decode_attention: %s", cudaGetErrorString(err));
-    }
-    kernel<<<grid, kThreads, smem, stream>>>(a);
-    return check_launch("bm_decode_attention");
-  };
-  const bool contig = a.hd % 32 == 0;
-  switch ((a.hd + 31) / 32) {
-    case 1: return contig ? go(attention_split_kernel<T, GM, 1, true>) : go(attention_split_kernel<T, GM, 1, false>);
-    case 2: return contig ? go(attention_split_kernel<T, GM, 2, true>) : go(attention_split_kernel<T, GM, 2, false>);
-    case 3: return go(attention_split_kernel<T, GM, 3, false>);
-    case 4: return contig ? go(attention_split_kernel<T, GM, 4, true>) : go(attention_split_kernel<T, GM, 4, false>);
-    case 5: return go(attention_split_kernel<T, GM, 5, false>);
-    case 6: return go(attention_split_kernel<T, GM, 6, false>);
-    case 7: return go(attention_split_kernel<T, GM, 7, false>);
-    default: return contig ? go(attention_split_kernel<T, GM, 8, true>) : go(attention_split_kernel<T, GM, 8, false>);
-  }
-}
 
-template <typename T>
-int launch(AttnArgs a, cudaStream_t stream) {
-  const size_t smem = sizeof(float) * (static_cast<size_t>(a.group) * a.hd + a.group * kThreads +
-                                       static_cast<size_t>(kWarps) * a.group * a.hd);
-  int st;
-  if (a.group <= 1) {
-    st = launch_group<T, 1>(a, smem, stream);
-  } else if (a.group <= 2) {
-    st = launch_group<T, 2>(a, smem, stream);
-  } else if (a.group <= 4) {
-    st = launch_group<T, 4>(a, smem, stream);
-  } else if (a.group <= 8) {
-    st = launch_group<T, 8>(a, smem, stream);
-  } else {
-    st = launch_group<T, 16>(a, smem, stream);
-  }
-  if (st != BM_OK || a.splits == 1) return st;
-  attention_combine_kernel<T><<<dim3(a.hq, static_cast<unsigned>(a.batch)), std::min(256, a.hd), 0, stream>>>(a);
-  return check_launch("bm_decode_attention (combine)");
-}
+}  // namespace attn
 
-}  // namespace
+using namespace attn;
+
 
 int decode_attention(void* out, const void* q, const void* k_cache, const void* v_cache, const int32_t* seq_ids,
                      const int32_t* lens, int32_t len0, int32_t max_len, int64_t batch, int32_t hq, int32_t hkv,
@@ -476,7 +106,7 @@ int decode_attention(void* out, const void* q, const void* k_cache, const void* 
   }
   a.ws = a.splits > 1 ? static_cast<float*>(workspace) : nullptr;
   cudaStream_t s = as_stream(stream);
-  return dtype == BM_F32 ? launch<float>(a, s) : launch<bf16>(a, s);
+  return dtype == BM_F32 ? launch_f32(a, s) : launch_bf16(a, s);
 }
 
 size_t decode_attention_workspace(int64_t batch, int32_t hq, int32_t hkv, int32_t hd, int32_t max_len) {

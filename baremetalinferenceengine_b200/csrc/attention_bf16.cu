@@ -1,0 +1,10 @@
+// Decode-attention kernels for bf16 caches (see attention_kernels.cuh).
+#include "attention_kernels.cuh"
+
+namespace bm {
+namespace attn {
+
+int launch_bf16(const AttnArgs& a, cudaStream_t stream) { return launch<bf16>(a, stream); }
+
+}  // namespace attn
+}  // namespace bm
