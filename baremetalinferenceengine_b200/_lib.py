@@ -57,6 +57,9 @@ SIGNATURES = {
     "bm_decode_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int64,
                                     c_int32, c_int32, c_int32, c_int32, c_int32, c_float, c_void_p, ctypes.c_size_t,
                                     c_int, c_void_p, c_void_p]),
+    "bm_decode_attention_static_scratch": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                                   c_int32, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32,
+                                                   c_float, c_int, c_void_p, c_void_p]),
     "bm_kv_cache_create": (c_int, [c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_int,
                                    ctypes.POINTER(c_void_p)]),
     "bm_kv_cache_destroy": (c_int, [c_void_p]),

@@ -209,6 +209,24 @@ int bm_decode_attention(void* out, const void* q, const void* k_cache, const voi
                         int32_t num_seqs, float scale, void* workspace, size_t workspace_bytes,
                         bm_dtype_t dtype, int32_t* d_status, void* stream);
 
+/* Decode attention that allocates nothing, for callers that cannot call
+ * cudaMalloc (a host application whose own arena owns all device memory, a
+ * plugin in a process that reserved the GPU up front, a latency-critical path
+ * that cannot afford cudaMalloc's implicit synchronisation). No counterpart in
+ * the reference. Same arguments and results as bm_decode_attention, without the
+ * workspace: the split partials live in an 8 MiB array compiled into the
+ * library (one copy per GPU, held until the process exits). A batch whose split
+ * plan needs more than 8 MiB (bm_decode_attention_workspace_size) is rejected
+ * with BM_ERR_INVALID_ARGUMENT. The first call on a device looks up that
+ * device's copy of the array; make it before capturing any stream. All calls
+ * share the array: calls that overlap on the GPU race on it and must be
+ * serialised by the caller. */
+int bm_decode_attention_static_scratch(void* out, const void* q, const void* k_cache, const void* v_cache,
+                                       const int32_t* seq_ids, const int32_t* lens, int32_t max_len,
+                                       int64_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                       int32_t head_dim, int32_t max_seq, int32_t num_seqs, float scale,
+                                       bm_dtype_t dtype, int32_t* d_status, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Batch-aware static KV cache. Replaces the reference's KVCache
  * (include/kv_cache.h:10-40, src/kv_cache.cu:4-47), which allocates
