@@ -1,0 +1,481 @@
+// Tensor-core GEMMs for sm_100a: tcgen05.mma with operands staged by TMA and
+// fp32 accumulators in tensor memory (TMEM); bf16 in, bf16 out.
+//
+//   bm_gemm_swiglu: out[R][F] = silu(x · w_gate) * (x · w_up)
+//     the FFN front half of src/execution_engine.cu:122-124 (two launch_gemm
+//     calls, then launch_swiglu) as one kernel: the gate and up products never
+//     leave the SM, the SwiGLU runs in the epilogue.
+//   bm_gemm: c[M][N] = a · b, the GEMM of src/kernels.cu:83-121 (launch_gemm).
+// A operand [rows][K] row-major (K contiguous); weights [K][N] row-major (N
+// contiguous), the layout launch_gemm's B has (include/kernels.cuh:20).
+//
+// One persistent CTA per SM walks output tiles of 128 rows x 256 accumulator
+// columns (SwiGLU: 128 gate + 128 up columns of the same 128 outputs; plain:
+// 256 outputs). Six warps:
+//   warp 0     TMA producer: per 64-wide K step, one 128x64 A box and four 64x64
+//              weight boxes (128-byte swizzle) into a 4-stage shared-memory ring;
+//   warp 1     owns the TMEM allocation (512 columns: two accumulators); one
+//              thread issues tcgen05.mma (M=128, N=256, K=16; A K-major, B
+//              MN-major) and commits each stage back to the producer and each
+//              finished accumulator to the epilogue;
+//   warps 2-5  epilogue: tcgen05.ld of their 32 TMEM lanes (one row each),
+//              SwiGLU or conversion, 16-byte stores; the accumulator is handed
+//              back so the next tile's MMAs overlap this tile's epilogue.
+// Every wait on an mbarrier is bounded in time: past kWaitLimitNs the CTA sets
+// BM_DEVERR_TIMEOUT in the status word, lets its copies and MMAs in flight land
+// (again bounded), frees its TMEM and returns.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "bm_common.cuh"
+#include "bm_host.h"
+
+namespace bm {
+namespace gemm {
+
+constexpr int kBlockM = 128;       // output rows per tile (TMEM lanes)
+constexpr int kBlockN = 256;       // accumulator columns per tile (MMA N)
+constexpr int kBlockK = 64;        // K per stage: one 128-byte swizzle row of bf16
+constexpr int kStages = 4;
+constexpr int kBoxN = 64;          // weight box width (128 bytes of bf16)
+constexpr int kABytes = kBlockM * kBlockK * 2;                 // 16 KB
+constexpr int kBBoxBytes = kBlockK * kBoxN * 2;                // 8 KB
+constexpr int kBBytes = kBBoxBytes * (kBlockN / kBoxN);        // 32 KB
+constexpr int kStageBytes = kABytes + kBBytes;                 // 48 KB
+constexpr int kThreads = 192;
+constexpr int kEpilogueThreads = 128;
+constexpr int kTmemCols = 2 * kBlockN;
+constexpr int kSmemBytes = kStages * kStageBytes + 1024 /* alignment slack */ + 256 /* barriers */;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s: far above any legitimate wait
+constexpr uint64_t kDrainLimitNs = 200000000ull;   // 0.2 s for copies in flight at exit
+constexpr int kGroupM = 16;        // tile order: 16 row blocks advance together (L2 reuse)
+
+struct Args {
+  void* out;
+  int64_t rows;
+  int n;          // output columns
+  int k;
+  int m_blocks, n_blocks, k_steps;
+  int32_t* status;
+};
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Waits until the phase of `bar` with parity `parity` has completed. Returns
+// false when another role has aborted, or (setting the abort flag and the status
+// bit) when `limit_ns` passes; `honour_abort` = false waits out the limit anyway.
+__device__ __noinline__ bool wait_phase(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int32_t* status,
+                                        uint64_t limit_ns, bool honour_abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 31) == 0) {
+      if (honour_abort && *abort_flag) return false;
+      if (global_ns() - t0 > limit_ns) {
+        *abort_flag = 1;
+        raise_status(status, BM_DEVERR_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] * B[smem], kind::f16 (bf16 operands, fp32 accumulator).
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrives once on `bar` when every MMA this thread issued so far has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (tcgen05 format): start, leading and stride
+// byte offsets in 16-byte units, descriptor version 1, 128-byte swizzle.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor: fp32 accumulator, bf16 A and B, A K-major, B
+// MN-major, N = kBlockN, M = kBlockM.
+constexpr uint32_t kInstrDesc = (1u << 4) | (1u << 7) | (1u << 10) | (0u << 15) | (1u << 16) |
+                                (static_cast<uint32_t>(kBlockN >> 3) << 17) |
+                                (static_cast<uint32_t>(kBlockM >> 4) << 24);
+
+__device__ __forceinline__ float silu(float g) { return __fdividef(g, 1.0f + exp2f(g * -1.4426950408889634f)); }
+
+// Tile t -> (row block, column block): kGroupM row blocks advance through the
+// column blocks together, so concurrently running CTAs share A and B tiles in L2.
+__device__ __forceinline__ void tile_coords(const Args& a, int t, int* mb, int* nb) {
+  const int per_group = kGroupM * a.n_blocks;
+  const int group = t / per_group;
+  const int first_m = group * kGroupM;
+  const int group_m = min(a.m_blocks - first_m, kGroupM);
+  const int r = t - group * per_group;
+  *mb = first_m + r % group_m;
+  *nb = r / group_m;
+}
+
+// SWIGLU: tb0 = w_gate, tb1 = w_up, 128 output columns per tile.
+// Otherwise tb0 = tb1 = b, 256 output columns per tile.
+template <bool SWIGLU>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb0,
+                   const __grid_constant__ CUtensorMap tb1, const Args a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // stages 1024-byte aligned (the swizzle atom); barriers after them
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                         ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* mma_done = acc_empty + 2;
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_s + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles = a.m_blocks * a.n_blocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], kEpilogueThreads);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_base_s)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_s;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t last_parity[kStages];
+    bool filled[kStages];
+    for (int s = 0; s < kStages; ++s) filled[s] = false;
+    bool ok = true;
+    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      int mb, nb;
+      tile_coords(a, t, &mb, &nb);
+      const int m0 = mb * kBlockM;
+      const int n0 = nb * (SWIGLU ? kBlockN / 2 : kBlockN);
+      for (int ks = 0; ks < a.k_steps; ++ks) {
+        if (!wait_phase(&empty[stage], phase ^ 1u, abort_flag, a.status, kWaitLimitNs, true)) {
+          ok = false;
+          break;
+        }
+        unsigned char* sa = smem + stage * kStageBytes;
+        unsigned char* sb = sa + kABytes;
+        mbar_expect_tx(&full[stage], kStageBytes);
+        const int k0 = ks * kBlockK;
+        tma_load_2d(sa, &ta, &full[stage], k0, m0);
+        if (SWIGLU) {
+          tma_load_2d(sb, &tb0, &full[stage], n0, k0);
+          tma_load_2d(sb + kBBoxBytes, &tb0, &full[stage], n0 + kBoxN, k0);
+          tma_load_2d(sb + 2 * kBBoxBytes, &tb1, &full[stage], n0, k0);
+          tma_load_2d(sb + 3 * kBBoxBytes, &tb1, &full[stage], n0 + kBoxN, k0);
+        } else {
+#pragma unroll
+          for (int j = 0; j < kBlockN / kBoxN; ++j) tma_load_2d(sb + j * kBBoxBytes, &tb0, &full[stage], n0 + j * kBoxN, k0);
+        }
+        filled[stage] = true;
+        last_parity[stage] = phase;
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    // let every copy in flight land before the CTA can exit
+    for (int s = 0; s < kStages; ++s) {
+      if (filled[s]) wait_phase(&full[s], last_parity[s], abort_flag, a.status, kDrainLimitNs, false);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool issued = false, ok = true;
+    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      if (!wait_phase(&acc_empty[acc], acc_phase ^ 1u, abort_flag, a.status, kWaitLimitNs, true)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBlockN);
+      for (int ks = 0; ks < a.k_steps; ++ks) {
+        if (!wait_phase(&full[stage], phase, abort_flag, a.status, kWaitLimitNs, true)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + stage * kStageBytes);
+        const uint32_t sb = sa + kABytes;
+#pragma unroll
+        for (int kk = 0; kk < kBlockK / 16; ++kk) {
+          // A: K-major, 16 K-elements = 32 bytes further along each swizzled row
+          const uint64_t a_desc = smem_desc(sa + kk * 32, 16, 1024);
+          // B: MN-major, 16 K-rows = two 8-row groups of 1024 bytes further on;
+          // 64-column blocks kBBoxBytes apart
+          const uint64_t b_desc = smem_desc(sb + kk * 2048, kBBoxBytes, 1024);
+          mma_bf16(d_tmem, a_desc, b_desc, kInstrDesc, (ks | kk) != 0 ? 1u : 0u);
+        }
+        issued = true;
+        mma_commit(&empty[stage]);  // the stage is free once these MMAs have read it
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      mma_commit(&acc_full[acc]);  // the accumulator is complete once every MMA so far has finished
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (issued) {  // no MMA may still write TMEM when it is freed
+      mma_commit(mma_done);
+      wait_phase(mma_done, 0, abort_flag, a.status, kDrainLimitNs, false);
+    }
+  } else if (warp >= 2) {
+    // ---------------- epilogue ----------------
+    const int quarter = warp & 3;  // TMEM lanes [32 * quarter, 32 * quarter + 32) belong to this warp
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      // one lane waits; the shuffle hands its verdict to the warp and reconverges
+      // it for the warp-wide tcgen05.ld
+      int ok = 1;
+      if (lane == 0) ok = wait_phase(&acc_full[acc], acc_phase, abort_flag, a.status, kWaitLimitNs, true);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      int mb, nb;
+      tile_coords(a, t, &mb, &nb);
+      const int64_t row = static_cast<int64_t>(mb) * kBlockM + quarter * 32 + lane;
+      const uint32_t tbase = tmem_base + lane_addr + static_cast<uint32_t>(acc * kBlockN);
+      constexpr int kOutCols = SWIGLU ? kBlockN / 2 : kBlockN;
+      const int n0 = nb * kOutCols;
+#pragma unroll 1
+      for (int c = 0; c < kOutCols; c += 32) {
+        uint32_t g[32];
+        float o[32];
+        tmem_load32(tbase + c, g);
+        if (SWIGLU) {
+          uint32_t u[32];
+          tmem_load32(tbase + kOutCols + c, u);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = silu(__uint_as_float(g[i])) * __uint_as_float(u[i]);
+        } else {
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(g[i]);
+        }
+        if (row < a.rows) {
+          __nv_bfloat16* dst = out + row * a.n + n0 + c;
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            if (n0 + c + v * 8 < a.n) st_plain(dst + v * 8, pack16<__nv_bfloat16>(o + v * 8));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// The driver's tensor-map encoder, looked up once through the runtime.
+EncodeTiled encoder() {
+  static std::once_flag once;
+  static EncodeTiled fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiled>(p);
+    }
+  });
+  return fn;
+}
+
+// A 2-D bf16 tensor map over [outer][inner] (row stride `inner` elements) with
+// a box of box_outer rows x box_inner columns and 128-byte swizzle; reads
+// outside the tensor return zeros.
+int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+             uint32_t box_outer, const char* what) {
+  EncodeTiled enc = encoder();
+  if (enc == nullptr) return fail(BM_ERR_CUDA, "%s: cuTensorMapEncodeTiled is not available", what);
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {inner * 2};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t elem[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, elem,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(BM_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
+  return BM_OK;
+}
+
+int check_shapes(const char* what, int64_t rows, int64_t n, int64_t k, bm_dtype_t dtype) {
+  if (dtype != BM_BF16) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: bf16 only (the tensor-core path takes bf16 operands)", what);
+  }
+  if (rows < 0 || rows > (int64_t{1} << 31) - kBlockM) return fail(BM_ERR_INVALID_ARGUMENT, "%s: bad row count", what);
+  if (n <= 0 || k <= 0 || n % 8 != 0 || k % 8 != 0 || n > (1 << 30) || k > (1 << 30)) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: N and K must be positive multiples of 8 (16-byte rows)", what);
+  }
+  return BM_OK;
+}
+
+template <bool SWIGLU>
+int run(const char* what, void* out, const void* x, const void* w0, const void* w1, int64_t rows, int n, int k,
+        int32_t* d_status, void* stream) {
+  if (!out || !x || !w0 || !w1) return fail(BM_ERR_INVALID_ARGUMENT, "%s: NULL pointer", what);
+  if (!aligned16(out) || !aligned16(x) || !aligned16(w0) || !aligned16(w1)) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: pointers must be 16-byte aligned", what);
+  }
+  if (rows == 0) return BM_OK;
+  CUtensorMap ta, tb0, tb1;
+  if (int st = make_map(&ta, x, static_cast<uint64_t>(k), static_cast<uint64_t>(rows), kBlockK, kBlockM, what)) return st;
+  if (int st = make_map(&tb0, w0, static_cast<uint64_t>(n), static_cast<uint64_t>(k), kBoxN, kBlockK, what)) return st;
+  if (int st = make_map(&tb1, w1, static_cast<uint64_t>(n), static_cast<uint64_t>(k), kBoxN, kBlockK, what)) return st;
+  Args a{};
+  a.out = out;
+  a.rows = rows;
+  a.n = n;
+  a.k = k;
+  a.m_blocks = static_cast<int>((rows + kBlockM - 1) / kBlockM);
+  const int out_cols = SWIGLU ? kBlockN / 2 : kBlockN;
+  a.n_blocks = (n + out_cols - 1) / out_cols;
+  a.k_steps = (k + kBlockK - 1) / kBlockK;
+  a.status = d_status;
+  const int64_t tiles = static_cast<int64_t>(a.m_blocks) * a.n_blocks;
+  if (tiles > (int64_t{1} << 31) - 1) return fail(BM_ERR_INVALID_ARGUMENT, "%s: too many tiles", what);
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, sm_count()));
+  auto kernel = gemm_tc_kernel<SWIGLU>;
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (err != cudaSuccess) return fail(BM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+  kernel<<<grid, kThreads, kSmemBytes, as_stream(stream)>>>(ta, tb0, tb1, a);
+  return check_launch(what);
+}
+
+}  // namespace gemm
+}  // namespace bm
+
+extern "C" int bm_gemm_swiglu(void* out, const void* x, const void* w_gate, const void* w_up, int64_t rows,
+                              int32_t dim, int32_t hidden, bm_dtype_t dtype, int32_t* d_status, void* stream) {
+  using namespace bm;
+  const char* what = "bm_gemm_swiglu";
+  if (int st = gemm::check_shapes(what, rows, hidden, dim, dtype)) return st;
+  return gemm::run<true>(what, out, x, w_gate, w_up, rows, hidden, dim, d_status, stream);
+}
+
+extern "C" int bm_gemm(void* c, const void* a, const void* b, int64_t m, int32_t n, int32_t k, bm_dtype_t dtype,
+                       int32_t* d_status, void* stream) {
+  using namespace bm;
+  const char* what = "bm_gemm";
+  if (int st = gemm::check_shapes(what, m, n, k, dtype)) return st;
+  return gemm::run<false>(what, c, a, b, b, m, n, k, d_status, stream);
+}

@@ -193,6 +193,49 @@ def add(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, st
     return out
 
 
+def gemm_swiglu(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, out: Optional[torch.Tensor] = None,
+                status: Optional[DeviceStatus] = None, stream=None) -> torch.Tensor:
+    """out = silu(x @ w_gate) * (x @ w_up) on the tensor cores (bf16): x [rows, dim],
+    w_gate and w_up [dim, hidden] (the reference's [in][out] weight layout)."""
+    for t, name in ((x, "x"), (w_gate, "w_gate"), (w_up, "w_up")):
+        _dense(t, name)
+    if x.dim() != 2 or w_gate.dim() != 2 or w_gate.shape != w_up.shape or w_gate.shape[0] != x.shape[1]:
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "need x [rows, dim] and w_gate, w_up [dim, hidden]")
+    rows, dim = x.shape
+    hidden = w_gate.shape[1]
+    if out is None:
+        out = torch.empty((rows, hidden), dtype=x.dtype, device=x.device)
+    _dense(out, "out")
+    _same(x, w_gate, w_up, out)
+    if tuple(out.shape) != (rows, hidden):
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "out must be [rows, hidden]")
+    with torch.cuda.device(_dev(x)):
+        check(load().bm_gemm_swiglu(_ptr(out), _ptr(x), _ptr(w_gate), _ptr(w_up), rows, dim, hidden, bm_dtype(x),
+                                    status.ptr if status else None, _stream(x.device, stream)))
+    return out
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None,
+         status: Optional[DeviceStatus] = None, stream=None) -> torch.Tensor:
+    """out = a @ b on the tensor cores (bf16): a [m, k], b [k, n] (launch_gemm's operand layout)."""
+    _dense(a, "a")
+    _dense(b, "b")
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "need a [m, k] and b [k, n]")
+    m, k = a.shape
+    n = b.shape[1]
+    if out is None:
+        out = torch.empty((m, n), dtype=a.dtype, device=a.device)
+    _dense(out, "out")
+    _same(a, b, out)
+    if tuple(out.shape) != (m, n):
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "out must be [m, n]")
+    with torch.cuda.device(_dev(a)):
+        check(load().bm_gemm(_ptr(out), _ptr(a), _ptr(b), m, n, k, bm_dtype(a), status.ptr if status else None,
+                             _stream(a.device, stream)))
+    return out
+
+
 def _positions(positions, rows):
     if isinstance(positions, int):
         return None, positions

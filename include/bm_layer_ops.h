@@ -56,6 +56,7 @@ typedef enum bm_status {
 #define BM_DEVERR_BAD_ID 0x1       /* token id outside [0, vocab) */
 #define BM_DEVERR_BAD_POSITION 0x2 /* position outside [0, max_seq) or beyond the RoPE table */
 #define BM_DEVERR_BAD_SEQUENCE 0x4 /* sequence id outside [0, num_seqs) */
+#define BM_DEVERR_TIMEOUT 0x8      /* a tensor-core pipeline wait passed its time limit; outputs incomplete */
 
 /* Human-readable name of a bm_status_t. Never NULL. */
 const char* bm_status_string(int status);
@@ -226,6 +227,24 @@ int bm_decode_attention_static_scratch(void* out, const void* q, const void* k_c
                                        int64_t batch, int32_t num_q_heads, int32_t num_kv_heads,
                                        int32_t head_dim, int32_t max_seq, int32_t num_seqs, float scale,
                                        bm_dtype_t dtype, int32_t* d_status, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Tensor-core GEMMs (tcgen05, bf16 operands, fp32 accumulation, bf16 output).
+ * The activation is [rows][K] row-major; weights are [K][N] row-major, the
+ * layout of launch_gemm's B operand (include/kernels.cuh:20, src/kernels.cu:83-121).
+ * N and K must be multiples of 8 and every pointer 16-byte aligned; any row
+ * count. BM_F32 is rejected (the tensor-core path takes bf16).
+ *
+ * bm_gemm_swiglu: out[r][f] = silu(sum_d x[r][d] w_gate[d][f]) * sum_d x[r][d] w_up[d][f]
+ * for x [rows][dim], w_gate and w_up [dim][hidden], out [rows][hidden]: the two
+ * FFN input projections and the SwiGLU of src/execution_engine.cu:122-124 in one
+ * kernel, the products kept in fp32 until the SwiGLU. bm_gemm: c[M][N] = a[M][K] b[K][N].
+ * A pipeline wait that passes its time limit (a fault, never a slow input) sets
+ * BM_DEVERR_TIMEOUT in *d_status. */
+int bm_gemm_swiglu(void* out, const void* x, const void* w_gate, const void* w_up, int64_t rows, int32_t dim,
+                   int32_t hidden, bm_dtype_t dtype, int32_t* d_status, void* stream);
+int bm_gemm(void* c, const void* a, const void* b, int64_t m, int32_t n, int32_t k, bm_dtype_t dtype,
+            int32_t* d_status, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Batch-aware static KV cache. Replaces the reference's KVCache

@@ -24,6 +24,10 @@
  *                       k and v (src/execution_engine.cu:113-115)
  *   oracle_gather       the row copy of src/execution_engine.cu:98-99 with the
  *                       id check of src/execution_engine.cu:63-65
+ *   oracle_decode_attention  tests/kernel_tests.cu:229-258 (test_attention), batched, GQA
+ *   oracle_gemm         tests/kernel_tests.cu:49-59 (reference_gemm)
+ *   oracle_gemm_swiglu  reference_gemm twice, then the SwiGLU of :122
+ *                       (src/execution_engine.cu:122-124)
  *   oracle_layer_step(_mt)  the five ops above (or a chosen subset) over a row
  *                       range, single- or multi-threaded: the timed CPU baseline.
  */
@@ -420,4 +424,111 @@ int32_t oracle_decode_attention(void* out, const void* q, const void* k_cache, c
   free(w);
   free(acc);
   return bad;
+}
+
+/* ------------------------------------------------------------------------- */
+/* GEMM (tests/kernel_tests.cu:49-59, reference_gemm; the product of           */
+/* src/kernels.cu:83-113): c[row][col] = sum_i a[row][i] * b[i][col], the sum  */
+/* in double over i = 0..k-1 in order, rounded once to the storage type.       */
+/* a [m][k], b [k][n], c [m][n], all row-major.                                */
+/* GEMM + SwiGLU (src/execution_engine.cu:122-124): gate and up are two such   */
+/* sums (b = w_gate, w_up) and out = gate / (1 + exp(-gate)) * up in double    */
+/* (the SwiGLU of tests/kernel_tests.cu:122), rounded once.                    */
+/* Rows are split over `threads` pthreads; each works through blocks of 16     */
+/* rows, widening each b row once per block.                                   */
+
+typedef struct {
+  void* c;
+  const void* a;
+  const void* b0;
+  const void* b1; /* NULL: plain GEMM */
+  int64_t r0, r1, n, k;
+  int dt;
+} GemmJob;
+
+#define GEMM_ROW_BLOCK 16
+
+static void gemm_rows(const GemmJob* j) {
+  const int64_t n = j->n, k = j->k;
+  const int sw = j->b1 != NULL;
+  double* bg = (double*)malloc(sizeof(double) * (size_t)(n > 0 ? n : 1));
+  double* bu = (double*)malloc(sizeof(double) * (size_t)(n > 0 ? n : 1));
+  double* g = (double*)malloc(sizeof(double) * (size_t)(GEMM_ROW_BLOCK * (n > 0 ? n : 1)));
+  double* u = (double*)malloc(sizeof(double) * (size_t)(GEMM_ROW_BLOCK * (n > 0 ? n : 1)));
+  for (int64_t rb = j->r0; rb < j->r1; rb += GEMM_ROW_BLOCK) {
+    const int64_t nr = (j->r1 - rb) < GEMM_ROW_BLOCK ? (j->r1 - rb) : GEMM_ROW_BLOCK;
+    for (int64_t x = 0; x < nr * n; ++x) g[x] = u[x] = 0.0;
+    for (int64_t i = 0; i < k; ++i) {
+      for (int64_t col = 0; col < n; ++col) bg[col] = ld(j->b0, i * n + col, j->dt);
+      if (sw) {
+        for (int64_t col = 0; col < n; ++col) bu[col] = ld(j->b1, i * n + col, j->dt);
+      }
+      for (int64_t r = 0; r < nr; ++r) {
+        const double av = ld(j->a, (rb + r) * k + i, j->dt);
+        double* gr = g + r * n;
+        for (int64_t col = 0; col < n; ++col) gr[col] += av * bg[col];
+        if (sw) {
+          double* ur = u + r * n;
+          for (int64_t col = 0; col < n; ++col) ur[col] += av * bu[col];
+        }
+      }
+    }
+    for (int64_t r = 0; r < nr; ++r) {
+      for (int64_t col = 0; col < n; ++col) {
+        const double gv = g[r * n + col];
+        const double v = sw ? gv / (1.0 + exp(-gv)) * u[r * n + col] : gv;
+        st(j->c, (rb + r) * n + col, v, j->dt);
+      }
+    }
+  }
+  free(bg);
+  free(bu);
+  free(g);
+  free(u);
+}
+
+static void* gemm_worker(void* arg) {
+  gemm_rows((const GemmJob*)arg);
+  return NULL;
+}
+
+static void gemm_mt(void* c, const void* a, const void* b0, const void* b1, int64_t m, int64_t n, int64_t k,
+                    int dt, int threads) {
+  if (threads < 1) threads = 1;
+  if (threads > m) threads = m > 0 ? (int)m : 1;
+  GemmJob* jobs = (GemmJob*)calloc((size_t)threads, sizeof(GemmJob));
+  pthread_t* tid = (pthread_t*)calloc((size_t)threads, sizeof(pthread_t));
+  int* started = (int*)calloc((size_t)threads, sizeof(int));
+  for (int t = 0; t < threads; ++t) {
+    jobs[t].c = c;
+    jobs[t].a = a;
+    jobs[t].b0 = b0;
+    jobs[t].b1 = b1;
+    jobs[t].r0 = m * t / threads;
+    jobs[t].r1 = m * (t + 1) / threads;
+    jobs[t].n = n;
+    jobs[t].k = k;
+    jobs[t].dt = dt;
+    if (t > 0) started[t] = pthread_create(&tid[t], NULL, gemm_worker, &jobs[t]) == 0;
+  }
+  gemm_rows(&jobs[0]);
+  for (int t = 1; t < threads; ++t) {
+    if (started[t]) {
+      pthread_join(tid[t], NULL);
+    } else {
+      gemm_rows(&jobs[t]); /* no thread: run its rows here */
+    }
+  }
+  free(started);
+  free(tid);
+  free(jobs);
+}
+
+void oracle_gemm(void* c, const void* a, const void* b, int64_t m, int64_t n, int64_t k, int dt, int threads) {
+  gemm_mt(c, a, b, NULL, m, n, k, dt, threads);
+}
+
+void oracle_gemm_swiglu(void* out, const void* x, const void* w_gate, const void* w_up, int64_t rows, int64_t dim,
+                        int64_t hidden, int dt, int threads) {
+  gemm_mt(out, x, w_gate, w_up, rows, hidden, dim, dt, threads);
 }

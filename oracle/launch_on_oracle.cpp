@@ -2,12 +2,13 @@
 // (include/kernels.cuh) served by the CPU oracle on host memory, for running
 // the reference's unmodified tests/kernel_tests.cu on a machine without a GPU
 // (with fake_cudart.cpp). The reference's own double-precision check loops then
-// grade the oracle: every in-scope check (rms_norm, swiglu, rope, add,
-// kv_store) prints its worst error against the oracle's output.
+// grade the oracle: every check that has an oracle counterpart (rms_norm,
+// swiglu, rope, add, kv_store, attention, gemm) prints its worst error against
+// the oracle's output.
 //
-// launch_gemm, launch_softmax(_batch) and launch_attention are outside the
-// layer-op path; plain loops stand in for them here only so the harness runs
-// to completion with the random-number sequence it was written with.
+// launch_softmax(_batch) is outside the path; a plain loop stands in for it
+// here only so the harness runs to completion with the random-number sequence
+// it was written with.
 #include <cmath>
 #include <cstdint>
 #include <vector>
@@ -26,6 +27,7 @@ int32_t oracle_kv_store(void* cache, const void* src, const int32_t* positions, 
 int32_t oracle_decode_attention(void* out, const void* q, const void* k_cache, const void* v_cache,
                                 const int32_t* seq_ids, const int32_t* lens, int64_t batch, int hq, int hkv, int hd,
                                 int max_seq, int num_seqs, int dt);
+void oracle_gemm(void* c, const void* a, const void* b, int64_t m, int64_t n, int64_t k, int dt, int threads);
 }
 
 void launch_rms_norm(float* out, float* in, float* weight, int size, float eps, cudaStream_t) {
@@ -51,14 +53,10 @@ void launch_kv_store(float* cache, float* src, int seq_pos, int num_heads, int h
 
 // ---- stand-ins outside the layer-op path ----
 
+// The oracle's GEMM, so that the harness's test_gemm grades it against the
+// reference's own reference_gemm.
 void launch_gemm(float* C, float* A, float* B, int M, int N, int K, cudaStream_t) {
-  for (int m = 0; m < M; ++m) {
-    for (int n = 0; n < N; ++n) {
-      double s = 0.0;
-      for (int k = 0; k < K; ++k) s += static_cast<double>(A[static_cast<size_t>(m) * K + k]) * B[static_cast<size_t>(k) * N + n];
-      C[static_cast<size_t>(m) * N + n] = static_cast<float>(s);
-    }
-  }
+  oracle_gemm(C, A, B, M, N, K, 0, 1);
 }
 
 void launch_softmax_batch(float* x, int size, int num_vectors, int stride, cudaStream_t) {

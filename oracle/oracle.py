@@ -74,6 +74,8 @@ def lib() -> ctypes.CDLL:
             "oracle_rope_table": (None, [vp, i32, cint, dbl]),
             "oracle_gather": (i32, [vp, vp, vp, i64, i64, i64, i64, cint]),
             "oracle_decode_attention": (i32, [vp, vp, vp, vp, vp, vp, i64, cint, cint, cint, cint, cint, cint]),
+            "oracle_gemm": (None, [vp, vp, vp, i64, i64, i64, cint, cint]),
+            "oracle_gemm_swiglu": (None, [vp, vp, vp, vp, i64, i64, i64, cint, cint]),
             "oracle_layer_step": (i32, [ctypes.POINTER(OracleStep), i64, i64]),
             "oracle_layer_step_mt": (i32, [ctypes.POINTER(OracleStep), i64, i64, cint]),
             "oracle_f32_to_bf16": (ctypes.c_uint16, [ctypes.c_float]),
@@ -221,6 +223,27 @@ def gather(table: np.ndarray, ids: np.ndarray, out: np.ndarray | None = None):
     return out, bad
 
 
+def gemm(a: np.ndarray, b: np.ndarray, threads: int = 1) -> np.ndarray:
+    """oracle_gemm (reference_gemm, tests/kernel_tests.cu:49-59): a [m, k] @ b [k, n]."""
+    a, b = _c(a), _c(b)
+    m, k = a.shape
+    n = b.shape[1]
+    c = np.empty((m, n), a.dtype)
+    lib().oracle_gemm(_p(c), _p(a), _p(b), m, n, k, _dt(a), threads)
+    return c
+
+
+def gemm_swiglu(x: np.ndarray, w_gate: np.ndarray, w_up: np.ndarray, threads: int = 1) -> np.ndarray:
+    """oracle_gemm_swiglu: silu(x @ w_gate) * (x @ w_up) in double, rounded once
+    (src/execution_engine.cu:122-124); x [rows, dim], weights [dim, hidden]."""
+    x, w_gate, w_up = _c(x), _c(w_gate), _c(w_up)
+    rows, dim = x.shape
+    hidden = w_gate.shape[1]
+    out = np.empty((rows, hidden), x.dtype)
+    lib().oracle_gemm_swiglu(_p(out), _p(x), _p(w_gate), _p(w_up), rows, dim, hidden, _dt(x), threads)
+    return out
+
+
 def layer_step(step: OracleStep, r0: int, r1: int, threads: int = 1) -> int:
     """oracle_layer_step(_mt) over rows [r0, r1): the timed CPU baseline."""
     if threads > 1:
@@ -255,6 +278,8 @@ def ref_lib() -> ctypes.CDLL:
         L = ctypes.CDLL(REF_CPU_LIB)
         L.ref_reference_rope.restype = None
         L.ref_reference_rope.argtypes = [vp, vp, cint, cint, cint, dbl]
+        L.ref_reference_gemm.restype = None
+        L.ref_reference_gemm.argtypes = [vp, vp, vp, cint, cint, cint]
         L.ref_kernel_tests_main.restype = cint
         L.ref_kernel_tests_main.argtypes = []
         _ref = L
@@ -268,3 +293,13 @@ def ref_reference_rope(x: np.ndarray, seq_pos: int, theta: float) -> np.ndarray:
     out = np.empty_like(x)
     ref_lib().ref_reference_rope(_p(out), _p(x), seq_pos, hd, heads, theta)
     return out
+
+
+def ref_reference_gemm(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """reference_gemm (tests/kernel_tests.cu:49-59) itself: a [m, k] @ b [k, n], float32."""
+    a, b = np.ascontiguousarray(a, np.float32), np.ascontiguousarray(b, np.float32)
+    m, k = a.shape
+    n = b.shape[1]
+    c = np.empty((m, n), np.float32)
+    ref_lib().ref_reference_gemm(_p(c), _p(a), _p(b), m, n, k)
+    return c

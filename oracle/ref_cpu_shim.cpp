@@ -18,3 +18,10 @@ extern "C" void ref_reference_rope(float* out, const float* x, int seq_pos, int 
 // The reference's whole kernel_tests main(), with its launch_* served by the
 // oracle; returns its exit status (0 = every check passed).
 extern "C" int ref_kernel_tests_main(void) { return reference_kernel_tests_main(); }
+
+// reference_gemm (tests/kernel_tests.cu:49-59): c [m][n] = a [m][k] * b [k][n], floats.
+extern "C" void ref_reference_gemm(float* c, const float* a, const float* b, int m, int n, int k) {
+  const std::vector<float> va(a, a + static_cast<size_t>(m) * k), vb(b, b + static_cast<size_t>(k) * n);
+  const std::vector<float> r = reference_gemm(va, vb, m, n, k);
+  std::copy(r.begin(), r.end(), c);
+}

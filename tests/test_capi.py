@@ -125,6 +125,15 @@ FAKE = 0x100000  # never dereferenced: every call below fails or returns before 
     lambda L: L.bm_kv_cache_layer(None, 0, ctypes.byref(ctypes.c_void_p()), ctypes.byref(ctypes.c_void_p())),
     lambda L: L.bm_kv_cache_seq_len(None, 0, ctypes.byref(ctypes.c_int32())),
     lambda L: L.bm_kv_cache_reset(None, 0),
+    lambda L: L.bm_gemm(FAKE, FAKE, FAKE, 4, 64, 64, 0, None, None),                  # fp32: tensor cores take bf16
+    lambda L: L.bm_gemm(FAKE, FAKE, FAKE, 3, 5, 7, 1, None, None),                    # N, K not multiples of 8
+    lambda L: L.bm_gemm(FAKE, FAKE, FAKE, 4, 64, 60, 1, None, None),                  # K not a multiple of 8
+    lambda L: L.bm_gemm(FAKE, FAKE, FAKE, -1, 64, 64, 1, None, None),                 # negative rows
+    lambda L: L.bm_gemm(FAKE, FAKE + 2, FAKE, 4, 64, 64, 1, None, None),              # misaligned operand
+    lambda L: L.bm_gemm(FAKE, None, FAKE, 4, 64, 64, 1, None, None),                  # NULL operand
+    lambda L: L.bm_gemm_swiglu(FAKE, FAKE, FAKE, FAKE, 4, 64, 64, 0, None, None),    # fp32
+    lambda L: L.bm_gemm_swiglu(FAKE, FAKE, FAKE, FAKE, 4, 64, 60, 1, None, None),    # hidden % 8
+    lambda L: L.bm_gemm_swiglu(FAKE, FAKE, FAKE, None, 4, 64, 64, 1, None, None),    # NULL w_up
 ])
 def test_host_checks_reject_before_any_launch(lib, call):
     assert call(lib) == _lib.BM_ERR_INVALID_ARGUMENT
@@ -143,6 +152,8 @@ def test_host_checks_reject_before_any_launch(lib, call):
     lambda L: L.bm_kv_store(FAKE, FAKE, None, 0, None, 0, 2, 8, 8, 1, 0, None, None),
     lambda L: L.bm_rope_table_destroy(None),
     lambda L: L.bm_kv_cache_destroy(None),
+    lambda L: L.bm_gemm(FAKE, FAKE, FAKE, 0, 64, 64, 1, None, None),
+    lambda L: L.bm_gemm_swiglu(FAKE, FAKE, FAKE, FAKE, 0, 64, 64, 1, None, None),
 ])
 def test_empty_calls_are_no_ops(lib, call):
     assert call(lib) == _lib.BM_OK

@@ -49,6 +49,10 @@ def test_reference_harness_grades_the_oracle():
         err = float(re.search(r"worst relative error (\S+)", line).group(1))
         # exact everywhere except the known-answer test, whose want rounds silu(-100)*2 (~7e-42) to 0
         assert err == 0.0 or ("stays finite" in line and err < 1e-40), line
+    gemm = [l for l in lines if l[6:].startswith("gemm")]
+    assert len(gemm) == 5, gemm  # kernel_tests.cu:263-267, served by oracle_gemm
+    for line in gemm:
+        assert line.startswith("PASS") and float(re.search(r"worst relative error (\S+)", line).group(1)) == 0.0, line
 
 
 @pytest.mark.parametrize("theta", [1e4, 5e5])
@@ -80,6 +84,46 @@ def test_golden_swiglu_known_answers():
             g, u = orc.f32_to_bf16(g), orc.f32_to_bf16(u)
         got = orc.swiglu(g, u)
         assert orc.worst_error(got, z["want"]) < 1e-30
+
+
+@pytest.mark.parametrize("m,n,k", [(16, 16, 16), (128, 128, 128), (3, 5, 7), (17, 33, 65), (1, 300, 200)])
+def test_oracle_gemm_is_reference_gemm(m, n, k):
+    _ensure_ref()
+    rng = np.random.default_rng(m * n + k)
+    a = rng.uniform(-1, 1, size=(m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, size=(k, n)).astype(np.float32)
+    want = orc.ref_reference_gemm(a, b)
+    for threads in (1, 4):
+        assert np.array_equal(orc.gemm(a, b, threads).view(np.uint32), want.view(np.uint32)), threads
+
+
+def test_golden_gemm_fixtures():
+    z = np.load(os.path.join(GOLDEN, "gemm_reference.npz"))
+    for n in range(int(z["count"])):
+        a, b = orc.bf16_to_f32(z[f"a{n}"]), orc.bf16_to_f32(z[f"b{n}"])
+        assert np.array_equal(orc.gemm(a, b).view(np.uint32), z[f"c{n}"].view(np.uint32)), n
+        # in bf16 storage the oracle rounds the same double sums once more, to bf16
+        got16 = orc.gemm(z[f"a{n}"], z[f"b{n}"])
+        assert np.array_equal(got16, orc.f32_to_bf16(z[f"c{n}"])) or orc.worst_error(got16, z[f"c{n}"]) <= 2.0 ** -8
+
+
+def test_oracle_gemm_swiglu_is_gemm_then_swiglu():
+    z = np.load(os.path.join(GOLDEN, "gemm_reference.npz"))
+    x, wg, wu = (orc.bf16_to_f32(z[k]) for k in ("ffn_x", "ffn_w_gate", "ffn_w_up"))
+    assert np.array_equal(orc.gemm(x, wg).view(np.uint32), z["ffn_gate"].view(np.uint32))
+    assert np.array_equal(orc.gemm(x, wu).view(np.uint32), z["ffn_up"].view(np.uint32))
+    fused = orc.gemm_swiglu(x, wg, wu, threads=3)
+    # the fused oracle keeps gate and up in double; rounding them to fp32 first moves the result by ~1 ulp
+    assert orc.worst_error(fused, orc.swiglu(z["ffn_gate"], z["ffn_up"])) < 1e-6
+    # known answers through the GEMM: x = e0, so gate and up are the first weight rows
+    gate = np.zeros((8, 8), np.float32)
+    gate[0, :5] = [-1000.0, -100.0, 0.0, 100.0, 1000.0]
+    up = np.zeros((8, 8), np.float32)
+    up[0, :5] = 2.0
+    e0 = np.zeros((1, 8), np.float32)
+    e0[0, 0] = 1.0
+    out = orc.gemm_swiglu(e0, gate, up)
+    assert orc.worst_error(out[0, :5], np.array([0.0, 0.0, 0.0, 200.0, 2000.0], np.float32)) < 1e-30
 
 
 def test_bf16_rounding_matches_torch():
