@@ -106,6 +106,7 @@ int decode_attention(void* out, const void* q, const void* k_cache, const void* 
   }
   a.ws = a.splits > 1 ? static_cast<float*>(workspace) : nullptr;
   cudaStream_t s = as_stream(stream);
+  if (tc_eligible(a, dtype)) return launch_tc(a, s);
   return dtype == BM_F32 ? launch_f32(a, s) : launch_bf16(a, s);
 }
 

@@ -398,5 +398,9 @@ int launch(AttnArgs a, cudaStream_t stream) {
 int launch_f32(const AttnArgs& a, cudaStream_t stream);
 int launch_bf16(const AttnArgs& a, cudaStream_t stream);
 
+// The tensor-core kernel (attention_tc.cu): bf16 caches with head_dim 128.
+bool tc_eligible(const AttnArgs& a, bm_dtype_t dtype);
+int launch_tc(const AttnArgs& a, cudaStream_t stream);
+
 }  // namespace attn
 }  // namespace bm

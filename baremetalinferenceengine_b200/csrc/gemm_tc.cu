@@ -27,13 +27,16 @@
 #include <cuda.h>
 
 #include <algorithm>
-#include <mutex>
 
 #include "bm_common.cuh"
 #include "bm_host.h"
+#include "bm_tc.cuh"
+#include "bm_tma.h"
 
 namespace bm {
 namespace gemm {
+
+using namespace bm::tc;
 
 constexpr int kBlockM = 128;       // output rows per tile (TMEM lanes)
 constexpr int kBlockN = 256;       // accumulator columns per tile (MMA N)
@@ -61,110 +64,10 @@ struct Args {
   int32_t* status;
 };
 
-// ---------------------------------------------------------------------------
-// PTX wrappers
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
-// Waits until the phase of `bar` with parity `parity` has completed. Returns
-// false when another role has aborted, or (setting the abort flag and the status
-// bit) when `limit_ns` passes; `honour_abort` = false waits out the limit anyway.
-__device__ __noinline__ bool wait_phase(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int32_t* status,
-                                        uint64_t limit_ns, bool honour_abort) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 31) == 0) {
-      if (honour_abort && *abort_flag) return false;
-      if (global_ns() - t0 > limit_ns) {
-        *abort_flag = 1;
-        raise_status(status, BM_DEVERR_TIMEOUT);
-        return false;
-      }
-    }
-  }
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
-      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// D[tmem] (+)= A[smem] * B[smem], kind::f16 (bf16 operands, fp32 accumulator).
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Arrives once on `bar` when every MMA this thread issued so far has completed.
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-// 32 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// Shared-memory matrix descriptor (tcgen05 format): start, leading and stride
-// byte offsets in 16-byte units, descriptor version 1, 128-byte swizzle.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-  return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
-         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
-}
 
 // Instruction descriptor: fp32 accumulator, bf16 A and B, A K-major, B
 // MN-major, N = kBlockN, M = kBlockM.
-constexpr uint32_t kInstrDesc = (1u << 4) | (1u << 7) | (1u << 10) | (0u << 15) | (1u << 16) |
-                                (static_cast<uint32_t>(kBlockN >> 3) << 17) |
-                                (static_cast<uint32_t>(kBlockM >> 4) << 24);
+constexpr uint32_t kInstrDesc = instr_desc_bf16(false, true, kBlockN, kBlockM);
 
 __device__ __forceinline__ float silu(float g) { return __fdividef(g, 1.0f + exp2f(g * -1.4426950408889634f)); }
 
@@ -212,14 +115,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    fence_barrier_init();
   }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_base_s)),
-                 "r"(kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
+  if (warp == 1) tmem_alloc(tmem_base_s, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -373,50 +271,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
-                 : "memory");
+    tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
 // ---------------------------------------------------------------------------
 // Host side
-
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-// The driver's tensor-map encoder, looked up once through the runtime.
-EncodeTiled encoder() {
-  static std::once_flag once;
-  static EncodeTiled fn = nullptr;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess) {
-      fn = reinterpret_cast<EncodeTiled>(p);
-    }
-  });
-  return fn;
-}
-
-// A 2-D bf16 tensor map over [outer][inner] (row stride `inner` elements) with
-// a box of box_outer rows x box_inner columns and 128-byte swizzle; reads
-// outside the tensor return zeros.
-int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
-             uint32_t box_outer, const char* what) {
-  EncodeTiled enc = encoder();
-  if (enc == nullptr) return fail(BM_ERR_CUDA, "%s: cuTensorMapEncodeTiled is not available", what);
-  const cuuint64_t dims[2] = {inner, outer};
-  const cuuint64_t strides[1] = {inner * 2};
-  const cuuint32_t box[2] = {box_inner, box_outer};
-  const cuuint32_t elem[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, elem,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(BM_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
-  return BM_OK;
-}
 
 int check_shapes(const char* what, int64_t rows, int64_t n, int64_t k, bm_dtype_t dtype) {
   if (dtype != BM_BF16) {
@@ -438,9 +298,9 @@ int run(const char* what, void* out, const void* x, const void* w0, const void* 
   }
   if (rows == 0) return BM_OK;
   CUtensorMap ta, tb0, tb1;
-  if (int st = make_map(&ta, x, static_cast<uint64_t>(k), static_cast<uint64_t>(rows), kBlockK, kBlockM, what)) return st;
-  if (int st = make_map(&tb0, w0, static_cast<uint64_t>(n), static_cast<uint64_t>(k), kBoxN, kBlockK, what)) return st;
-  if (int st = make_map(&tb1, w1, static_cast<uint64_t>(n), static_cast<uint64_t>(k), kBoxN, kBlockK, what)) return st;
+  if (int st = make_tensor_map_bf16(&ta, x, static_cast<uint64_t>(k), static_cast<uint64_t>(rows), kBlockK, kBlockM, what)) return st;
+  if (int st = make_tensor_map_bf16(&tb0, w0, static_cast<uint64_t>(n), static_cast<uint64_t>(k), kBoxN, kBlockK, what)) return st;
+  if (int st = make_tensor_map_bf16(&tb1, w1, static_cast<uint64_t>(n), static_cast<uint64_t>(k), kBoxN, kBlockK, what)) return st;
   Args a{};
   a.out = out;
   a.rows = rows;
