@@ -27,10 +27,12 @@
 namespace bm {
 namespace attn {
 
-void plan_splits(int64_t pairs, int max_len, int sms, int* splits, int* split_len) {
+// min_tiles: the fewest tiles a split may hold (the tensor-core kernel pays a
+// fixed start-up per CTA, so its splits keep at least four tiles).
+void plan_splits(int64_t pairs, int max_len, int sms, int* splits, int* split_len, int min_tiles = 1) {
   const int tiles = (max_len + kThreads - 1) / kThreads;
   const int64_t want = std::max<int64_t>(1, (static_cast<int64_t>(sms) * 4 + pairs - 1) / pairs);
-  const int n = static_cast<int>(std::min<int64_t>(want, tiles));
+  const int n = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, tiles / std::max(min_tiles, 1))));
   const int tiles_per_split = (tiles + n - 1) / n;
   *split_len = tiles_per_split * kThreads;
   *splits = (tiles + tiles_per_split - 1) / tiles_per_split;
@@ -93,7 +95,8 @@ int decode_attention(void* out, const void* q, const void* k_cache, const void* 
   a.num_seqs = num_seqs;
   a.qscale = scale * 1.4426950408889634f;  // scores in base 2: exp(x) = exp2(x * log2(e))
   a.status = d_status;
-  plan_splits(batch * hkv, max_len, sm_count(), &a.splits, &a.split_len);
+  const bool tc = tc_eligible(a, dtype);
+  plan_splits(batch * hkv, max_len, sm_count(), &a.splits, &a.split_len, tc ? 4 : 1);
   const size_t need = workspace_bytes(batch, hkv, a.group, hd, a.splits);
   if (need > 0 && (workspace == nullptr || workspace_size < need)) {
     // Less scratch than the plan wants: as many splits as it holds (maybe one).
@@ -106,7 +109,7 @@ int decode_attention(void* out, const void* q, const void* k_cache, const void* 
   }
   a.ws = a.splits > 1 ? static_cast<float*>(workspace) : nullptr;
   cudaStream_t s = as_stream(stream);
-  if (tc_eligible(a, dtype)) return launch_tc(a, s);
+  if (tc) return launch_tc(a, s);
   return dtype == BM_F32 ? launch_f32(a, s) : launch_bf16(a, s);
 }
 

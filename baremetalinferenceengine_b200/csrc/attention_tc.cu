@@ -52,7 +52,7 @@ constexpr int kOffP = kOffQ + kQBytes;                 // two P buffers
 constexpr int kOffMax = kOffP + 2 * kPBytes;           // [2][4][16] floats
 constexpr int kOffL = kOffMax + 2 * 4 * kTcN * 4;      // [4][16] floats
 constexpr int kOffBar = kOffL + 4 * kTcN * 4;
-constexpr int kNumBars = 2 * kTcStages + 6 * 2 + 1;
+constexpr int kNumBars = 2 * kTcStages + 5 * 2 + 1;
 constexpr int kTcSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024 /* alignment slack */;
 constexpr uint32_t kTmemCols = 64;
 constexpr uint64_t kWaitNs = 2000000000ull;
@@ -75,6 +75,24 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
+// The four softmax warps meet here once per tile (barrier 1, 128 threads); the
+// result is true when any of them saw the abort flag set, the same for all.
+__device__ __forceinline__ bool softmax_warps_sync_any(bool flag) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.or.pred p, 1, 128, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(flag))
+      : "memory");
+  return r != 0;
+}
+
+// GM: the group size rounded up to a power of two; the softmax works on GM
+// queries (the MMAs always on 16, the rows past GM of P stay zero).
+template <int GM>
 __global__ void __launch_bounds__(kTcThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                         const AttnArgs a) {
@@ -116,8 +134,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* pfull = sfree + 2;          // P written               (128)
   uint64_t* ofull = pfull + 2;          // mix MMA done            (commit)
   uint64_t* ofree = ofull + 2;          // mix output read         (128)
-  uint64_t* mxbar = ofree + 2;          // tile maxima exchanged   (128)
-  uint64_t* mma_done = mxbar + 2;
+  uint64_t* mma_done = ofree + 2;
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_s + 1);
 
@@ -132,7 +149,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&pfull[i], kTcSoftmaxThreads);
       mbar_init(&ofull[i], 1);
       mbar_init(&ofree[i], kTcSoftmaxThreads);
-      mbar_init(&mxbar[i], kTcSoftmaxThreads);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -148,6 +164,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
       if (row < G) v = __ldg(reinterpret_cast<const uint4*>(qb + row * kTcHd + col));
       *reinterpret_cast<uint4*>(q_s + swz_offset(row, col, kTcN)) = v;
+    }
+    for (int c = t; c < 2 * kPBytes / 16; c += kTcSoftmaxThreads) {  // both P buffers start at zero
+      *reinterpret_cast<uint4*>(p_s + c * 16) = make_uint4(0u, 0u, 0u, 0u);
     }
     fence_proxy_async_smem();
   }
@@ -233,100 +252,87 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 
   // ---------------- softmax and accumulation (warps 2-5) ----------------
+  // A timed-out wait sets the abort flag and the warp carries on to the next
+  // tile barrier, where all four warps see the flag and leave together.
   const int quarter = warp & 3;
   const int t = quarter * 32 + lane;  // TMEM lane: tile position t (scores), dimension t (mix)
-  float m_run[kTcN], l_part[kTcN], acc[kTcN], alpha_prev[kTcN];
+  float m_run[GM], l_part[GM], acc[GM], alpha_prev[GM];
   if (warp >= 2) {
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
 #pragma unroll
-    for (int g = 0; g < kTcN; ++g) {
+    for (int g = 0; g < GM; ++g) {
       m_run[g] = -INFINITY;
       l_part[g] = 0.f;
       acc[g] = 0.f;
       alpha_prev[g] = 0.f;
     }
-    for (int i = 0; i <= n_tiles; ++i) {
-      if (i < n_tiles) {
-        if (!warp_wait(&sfull[i & 1], static_cast<uint32_t>((i >> 1) & 1), abort_flag, a.status)) break;
-        tc_fence_after();
-        uint32_t r[kTcN];
-        tmem_load16(tmem_base + lane_addr + (i & 1) * kTcN, r);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&sfree[i & 1]);
-        const int tile_start = start + i * kTcTile;
-        const bool valid = tile_start + t < end;
-        float s[kTcN];
+    auto accumulate = [&](int j) {  // tile j's mix output, rescaled by its own factor
+      warp_wait(&ofull[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, a.status);
+      tc_fence_after();
+      uint32_t o[kTcN];
+      tmem_load16(tmem_base + lane_addr + 2 * kTcN + (j & 1) * kTcN, o);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&ofree[j & 1]);
 #pragma unroll
-        for (int g = 0; g < kTcN; ++g) s[g] = valid ? __uint_as_float(r[g]) * a.qscale : -INFINITY;
-        // tile maxima: warp shuffles, then the four warps through shared memory
-        float* wm = wmax + (i & 1) * 4 * kTcN;
+      for (int g = 0; g < GM; ++g) acc[g] = fmaf(acc[g], alpha_prev[g], __uint_as_float(o[g]));
+    };
+    for (int i = 0; i < n_tiles; ++i) {
+      warp_wait(&sfull[i & 1], static_cast<uint32_t>((i >> 1) & 1), abort_flag, a.status);
+      tc_fence_after();
+      uint32_t r[kTcN];
+      tmem_load16(tmem_base + lane_addr + (i & 1) * kTcN, r);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&sfree[i & 1]);
+      const int tile_start = start + i * kTcTile;
+      const bool valid = tile_start + t < end;
+      float s[GM];
 #pragma unroll
-        for (int g = 0; g < kTcN; ++g) {
-          float v = s[g];
+      for (int g = 0; g < GM; ++g) s[g] = valid ? __uint_as_float(r[g]) * a.qscale : -INFINITY;
+      // tile maxima: warp shuffles, then the four warps through shared memory
+      float* wm = wmax + (i & 1) * 4 * kTcN;
 #pragma unroll
-          for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
-          if (lane == 0) wm[quarter * kTcN + g] = v;
-        }
-        mbar_arrive(&mxbar[i & 1]);
-        if (!warp_wait(&mxbar[i & 1], static_cast<uint32_t>((i >> 1) & 1), abort_flag, a.status)) break;
-        float alpha[kTcN];
-        bf16* pb = reinterpret_cast<bf16*>(p_s + (i & 1) * kPBytes);
+      for (int g = 0; g < GM; ++g) {
+        float v = s[g];
 #pragma unroll
-        for (int g = 0; g < kTcN; ++g) {
-          // every tile holds a valid position, so the tile maximum is finite
-          const float tmax = fmaxf(fmaxf(wm[g], wm[kTcN + g]), fmaxf(wm[2 * kTcN + g], wm[3 * kTcN + g]));
-          const float m_new = fmaxf(m_run[g], tmax);
-          alpha[g] = exp2f(m_run[g] - m_new);
-          m_run[g] = m_new;
-          const float p = (valid && g < G) ? exp2f(s[g] - m_new) : 0.f;
-          l_part[g] = l_part[g] * alpha[g] + p;
-          *reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(pb) + swz_offset(g, t, kTcN)) =
-              __float2bfloat16_rn(p);
-        }
-        if (!valid) {  // clear this stage's V row t, so stale cache contents cannot reach the mix
-          const int s_idx = i % kTcStages;
-          wait_phase(&full[s_idx], static_cast<uint32_t>((i / kTcStages) & 1), abort_flag, a.status, kWaitNs, true);
-          unsigned char* vrow = smem + s_idx * kStageBytes + 2 * kBoxBytes + t * 128;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0u, 0u, 0u, 0u);
-            *reinterpret_cast<uint4*>(vrow + kBoxBytes + c * 16) = make_uint4(0u, 0u, 0u, 0u);
-          }
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(&pfull[i & 1]);
-        if (i >= 1) {
-          // accumulate tile i - 1 with its own rescale factor, then keep this tile's
-          const int j = i - 1;
-          if (!warp_wait(&ofull[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, a.status)) break;
-          tc_fence_after();
-          uint32_t o[kTcN];
-          tmem_load16(tmem_base + lane_addr + 2 * kTcN + (j & 1) * kTcN, o);
-          tmem_wait_ld();
-          tc_fence_before();
-          mbar_arrive(&ofree[j & 1]);
-#pragma unroll
-          for (int g = 0; g < kTcN; ++g) acc[g] = fmaf(acc[g], alpha_prev[g], __uint_as_float(o[g]));
-        }
-#pragma unroll
-        for (int g = 0; g < kTcN; ++g) alpha_prev[g] = alpha[g];
-      } else {  // after the last tile: its mix output
-        const int j = i - 1;
-        if (!warp_wait(&ofull[j & 1], static_cast<uint32_t>((j >> 1) & 1), abort_flag, a.status)) break;
-        tc_fence_after();
-        uint32_t o[kTcN];
-        tmem_load16(tmem_base + lane_addr + 2 * kTcN + (j & 1) * kTcN, o);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&ofree[j & 1]);
-#pragma unroll
-        for (int g = 0; g < kTcN; ++g) acc[g] = fmaf(acc[g], alpha_prev[g], __uint_as_float(o[g]));
+        for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+        if (lane == 0) wm[quarter * kTcN + g] = v;
       }
+      if (softmax_warps_sync_any(*abort_flag != 0)) break;
+      float alpha[GM];
+      unsigned char* pb = p_s + (i & 1) * kPBytes;
+#pragma unroll
+      for (int g = 0; g < GM; ++g) {
+        // every tile holds a valid position, so the tile maximum is finite
+        const float tmax = fmaxf(fmaxf(wm[g], wm[kTcN + g]), fmaxf(wm[2 * kTcN + g], wm[3 * kTcN + g]));
+        const float m_new = fmaxf(m_run[g], tmax);
+        alpha[g] = exp2f(m_run[g] - m_new);
+        m_run[g] = m_new;
+        const float p = (valid && g < G) ? exp2f(s[g] - m_new) : 0.f;
+        l_part[g] = l_part[g] * alpha[g] + p;
+        *reinterpret_cast<bf16*>(pb + swz_offset(g, t, kTcN)) = __float2bfloat16_rn(p);
+      }
+      if (!valid) {  // clear this stage's V row t, so stale cache contents cannot reach the mix
+        const int s_idx = i % kTcStages;
+        wait_phase(&full[s_idx], static_cast<uint32_t>((i / kTcStages) & 1), abort_flag, a.status, kWaitNs, true);
+        unsigned char* vrow = smem + s_idx * kStageBytes + 2 * kBoxBytes + t * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+          *reinterpret_cast<uint4*>(vrow + kBoxBytes + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&pfull[i & 1]);
+      if (i >= 1) accumulate(i - 1);
+#pragma unroll
+      for (int g = 0; g < GM; ++g) alpha_prev[g] = alpha[g];
+      if (i == n_tiles - 1) accumulate(i);
     }
     // the row sums: each thread holds its positions' share
 #pragma unroll
-    for (int g = 0; g < kTcN; ++g) {
+    for (int g = 0; g < GM; ++g) {
       const float v = warp_sum(l_part[g]);
       if (lane == 0) lsum[quarter * kTcN + g] = v;
     }
@@ -335,7 +341,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   if (warp >= 2) {
 #pragma unroll
-    for (int g = 0; g < kTcN; ++g) {
+    for (int g = 0; g < GM; ++g) {
       if (g < G) {
         const float l = lsum[g] + lsum[kTcN + g] + lsum[2 * kTcN + g] + lsum[3 * kTcN + g];
         if (ws == nullptr) {
@@ -371,11 +377,26 @@ int launch_tc(const AttnArgs& a, cudaStream_t stream) {
   CUtensorMap tk, tv;
   if (int st = make_tensor_map_bf16(&tk, a.k_cache, kTcHd, rows, 64, kTcTile, what)) return st;
   if (int st = make_tensor_map_bf16(&tv, a.v_cache, kTcHd, rows, 64, kTcTile, what)) return st;
-  cudaError_t err = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes);
-  if (err != cudaSuccess) return fail(BM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
   const dim3 grid(a.splits, a.hkv, static_cast<unsigned>(a.batch));
-  attention_tc_kernel<<<grid, kTcThreads, kTcSmemBytes, stream>>>(tk, tv, a);
-  if (int st = check_launch(what)) return st;
+  auto go = [&](auto kernel) {
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes);
+    if (err != cudaSuccess) return fail(BM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+    kernel<<<grid, kTcThreads, kTcSmemBytes, stream>>>(tk, tv, a);
+    return check_launch(what);
+  };
+  int st;
+  if (a.group <= 1) {
+    st = go(attention_tc_kernel<1>);
+  } else if (a.group <= 2) {
+    st = go(attention_tc_kernel<2>);
+  } else if (a.group <= 4) {
+    st = go(attention_tc_kernel<4>);
+  } else if (a.group <= 8) {
+    st = go(attention_tc_kernel<8>);
+  } else {
+    st = go(attention_tc_kernel<16>);
+  }
+  if (st != BM_OK) return st;
   if (a.splits == 1) return BM_OK;
   attention_combine_kernel<bf16><<<dim3(a.hq, static_cast<unsigned>(a.batch)), std::min(256, a.hd), 0, stream>>>(a);
   return check_launch("bm_decode_attention (combine)");
