@@ -275,6 +275,225 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant for row counts above one row block: a cluster of two CTAs on
+// two SMs computes a 256-row tile with tcgen05.mma.cta_group::2 (M=256, N=256).
+// Each CTA loads its own 128 rows of A and its own half of B (SwiGLU: the leader
+// the 128 gate columns, the peer the 128 up columns; plain: 128 columns each), so
+// each SM reads 8 KB of operands per 128 cycles of math instead of 12 KB per 64,
+// and each CTA's accumulator holds gate and up of its own 128 rows. The leader's
+// producer posts the transaction bytes of both CTAs on the leader's full
+// barrier; both CTAs' copies count on it; one thread of the leader issues the
+// MMAs and commits to the barriers of both CTAs; both epilogues hand the
+// accumulator back through the leader's barrier. No load uses multicast.
+
+constexpr int kPairStages = 6;
+constexpr int kPairStageBytes = kABytes + kBBytes / 2;           // 16 KB of A + 16 KB of B: 32 KB
+constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 1024 + 256;
+constexpr int kGroupMPair = 8;     // tile order: 8 pair row blocks (2048 rows) advance together
+constexpr uint32_t kPairInstrDesc = instr_desc_bf16(false, true, kBlockN, 2 * kBlockM);
+
+__device__ __forceinline__ void pair_tile_coords(const Args& a, int t, int* mb, int* nb) {
+  const int per_group = kGroupMPair * a.n_blocks;
+  const int group = t / per_group;
+  const int first_m = group * kGroupMPair;
+  const int group_m = min(a.m_blocks - first_m, kGroupMPair);
+  const int r = t - group * per_group;
+  *mb = first_m + r % group_m;
+  *nb = r / group_m;
+}
+
+template <bool SWIGLU>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb0,
+                        const __grid_constant__ CUtensorMap tb1, const Args a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                         ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPairStages * kPairStageBytes);
+  uint64_t* empty = full + kPairStages;
+  uint64_t* acc_full = empty + kPairStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* mma_done = acc_empty + 2;
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_s + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0: the leader, which issues the MMAs
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int tiles = a.m_blocks * a.n_blocks;
+  constexpr int kOutCols = SWIGLU ? kBlockN / 2 : kBlockN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 2 * kEpilogueThreads);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_base_s, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any copy or arrival reaches them
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_s;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t last_parity[kPairStages];
+    bool filled[kPairStages];
+    for (int s = 0; s < kPairStages; ++s) filled[s] = false;
+    bool ok = true;
+    const CUtensorMap* tb = (SWIGLU && !leader) ? &tb1 : &tb0;
+    for (int t = pair; t < tiles && ok; t += npairs) {
+      int mb, nb;
+      pair_tile_coords(a, t, &mb, &nb);
+      const int m0 = mb * 2 * kBlockM + static_cast<int>(rank) * kBlockM;
+      const int n0 = SWIGLU ? nb * kOutCols : nb * kOutCols + static_cast<int>(rank) * (kBlockN / 2);
+      for (int ks = 0; ks < a.k_steps; ++ks) {
+        if (!wait_phase(&empty[stage], phase ^ 1u, abort_flag, a.status, kWaitLimitNs, true)) {
+          ok = false;
+          break;
+        }
+        unsigned char* sa = smem + stage * kPairStageBytes;
+        unsigned char* sb = sa + kABytes;
+        const uint32_t bar = cluster_addr(&full[stage], 0);
+        if (leader) mbar_expect_tx(&full[stage], 2 * kPairStageBytes);
+        const int k0 = ks * kBlockK;
+        tma_load_2d_pair(sa, &ta, bar, k0, m0);
+        tma_load_2d_pair(sb, tb, bar, n0, k0);
+        tma_load_2d_pair(sb + kBBoxBytes, tb, bar, n0 + kBoxN, k0);
+        filled[stage] = true;
+        last_parity[stage] = phase;
+        if (++stage == kPairStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (leader) {  // every copy of the pair counts on the leader's barriers: let them land
+      for (int s = 0; s < kPairStages; ++s) {
+        if (filled[s]) wait_phase(&full[s], last_parity[s], abort_flag, a.status, kDrainLimitNs, false);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer (leader) ----------------
+    bool issued = false;
+    if (leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += npairs) {
+        if (!wait_phase(&acc_empty[acc], acc_phase ^ 1u, abort_flag, a.status, kWaitLimitNs, true)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBlockN);
+        for (int ks = 0; ks < a.k_steps; ++ks) {
+          if (!wait_phase(&full[stage], phase, abort_flag, a.status, kWaitLimitNs, true)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * kPairStageBytes);
+          const uint32_t sb = sa + kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBlockK / 16; ++kk) {
+            const uint64_t a_desc = smem_desc(sa + kk * 32, 16, 1024);
+            const uint64_t b_desc = smem_desc(sb + kk * 2048, kBBoxBytes, 1024);
+            mma_bf16_pair(d_tmem, a_desc, b_desc, kPairInstrDesc, (ks | kk) != 0 ? 1u : 0u);
+          }
+          issued = true;
+          mma_commit_pair(&empty[stage], 0x3);  // both CTAs may refill this stage
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair(&acc_full[acc], 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // no pair MMA may still write either CTA's TMEM when it is freed: the leader
+      // drains them here, and the cluster barrier at the end holds the peer back
+      if (issued) {
+        mma_commit_pair(mma_done, 0x3);
+        wait_phase(mma_done, 0, abort_flag, a.status, kDrainLimitNs, false);
+      }
+    }
+  } else if (warp >= 2) {
+    // ---------------- epilogue (both CTAs) ----------------
+    const int quarter = warp & 3;
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
+    for (int t = pair; t < tiles; t += npairs) {
+      int ok = 1;
+      if (lane == 0) ok = wait_phase(&acc_full[acc], acc_phase, abort_flag, a.status, kWaitLimitNs, true);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      int mb, nb;
+      pair_tile_coords(a, t, &mb, &nb);
+      const int64_t row = static_cast<int64_t>(mb) * 2 * kBlockM + rank * kBlockM + quarter * 32 + lane;
+      const uint32_t tbase = tmem_base + lane_addr + static_cast<uint32_t>(acc * kBlockN);
+      const int n0 = nb * kOutCols;
+#pragma unroll 1
+      for (int c = 0; c < kOutCols; c += 32) {
+        uint32_t g[32];
+        float o[32];
+        tmem_load32(tbase + c, g);
+        if (SWIGLU) {
+          uint32_t u[32];
+          tmem_load32(tbase + kOutCols + c, u);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = silu(__uint_as_float(g[i])) * __uint_as_float(u[i]);
+        } else {
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(g[i]);
+        }
+        if (row < a.rows) {
+          __nv_bfloat16* dst = out + row * a.n + n0 + c;
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            if (n0 + c + v * 8 < a.n) st_plain(dst + v * 8, pack16<__nv_bfloat16>(o + v * 8));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(cluster_addr(&acc_empty[acc], 0));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA leaves while the other may still reach its shared memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 
@@ -306,13 +525,24 @@ int run(const char* what, void* out, const void* x, const void* w0, const void* 
   a.rows = rows;
   a.n = n;
   a.k = k;
-  a.m_blocks = static_cast<int>((rows + kBlockM - 1) / kBlockM);
+  // more than one row block: CTA pairs with 256-row tiles; otherwise single CTAs
+  const bool paired = rows > kBlockM && sm_count() >= 2;
+  const int block_rows = paired ? 2 * kBlockM : kBlockM;
+  a.m_blocks = static_cast<int>((rows + block_rows - 1) / block_rows);
   const int out_cols = SWIGLU ? kBlockN / 2 : kBlockN;
   a.n_blocks = (n + out_cols - 1) / out_cols;
   a.k_steps = (k + kBlockK - 1) / kBlockK;
   a.status = d_status;
   const int64_t tiles = static_cast<int64_t>(a.m_blocks) * a.n_blocks;
   if (tiles > (int64_t{1} << 31) - 1) return fail(BM_ERR_INVALID_ARGUMENT, "%s: too many tiles", what);
+  if (paired) {
+    const int grid = 2 * static_cast<int>(std::min<int64_t>(tiles, sm_count() / 2));
+    auto kernel = gemm_tc_pair_kernel<SWIGLU>;
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes);
+    if (err != cudaSuccess) return fail(BM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+    kernel<<<grid, kThreads, kPairSmemBytes, as_stream(stream)>>>(ta, tb0, tb1, a);
+    return check_launch(what);
+  }
   const int grid = static_cast<int>(std::min<int64_t>(tiles, sm_count()));
   auto kernel = gemm_tc_kernel<SWIGLU>;
   cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
