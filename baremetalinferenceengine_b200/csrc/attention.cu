@@ -96,7 +96,8 @@ int decode_attention(void* out, const void* q, const void* k_cache, const void* 
   a.qscale = scale * 1.4426950408889634f;  // scores in base 2: exp(x) = exp2(x * log2(e))
   a.status = d_status;
   const bool tc = tc_eligible(a, dtype);
-  plan_splits(batch * hkv, max_len, sm_count(), &a.splits, &a.split_len, tc ? 4 : 1);
+  plan_splits(batch * hkv, max_len, sm_count(), &a.splits, &a.split_len,
+              tc || f32_tma_eligible(a, dtype) ? 4 : 1);
   const size_t need = workspace_bytes(batch, hkv, a.group, hd, a.splits);
   if (need > 0 && (workspace == nullptr || workspace_size < need)) {
     // Less scratch than the plan wants: as many splits as it holds (maybe one).
@@ -110,6 +111,7 @@ int decode_attention(void* out, const void* q, const void* k_cache, const void* 
   a.ws = a.splits > 1 ? static_cast<float*>(workspace) : nullptr;
   cudaStream_t s = as_stream(stream);
   if (tc) return launch_tc(a, s);
+  if (f32_tma_eligible(a, dtype)) return launch_f32_tma(a, s);
   return dtype == BM_F32 ? launch_f32(a, s) : launch_bf16(a, s);
 }
 

@@ -402,5 +402,9 @@ int launch_bf16(const AttnArgs& a, cudaStream_t stream);
 bool tc_eligible(const AttnArgs& a, bm_dtype_t dtype);
 int launch_tc(const AttnArgs& a, cudaStream_t stream);
 
+// The TMA-fed CUDA-core kernel (attention_f32_tma.cu): fp32 caches with head_dim 128.
+bool f32_tma_eligible(const AttnArgs& a, bm_dtype_t dtype);
+int launch_f32_tma(const AttnArgs& a, cudaStream_t stream);
+
 }  // namespace attn
 }  // namespace bm

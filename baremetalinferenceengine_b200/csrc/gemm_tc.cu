@@ -288,10 +288,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 // MMAs and commits to the barriers of both CTAs; both epilogues hand the
 // accumulator back through the leader's barrier. No load uses multicast.
 
-constexpr int kPairStages = 6;
+#ifndef BM_GEMM_PAIR_STAGES
+#define BM_GEMM_PAIR_STAGES 6  // 6 x 32 KB (7 fit; measured no faster)
+#endif
+#ifndef BM_GEMM_PAIR_GROUP_M
+#define BM_GEMM_PAIR_GROUP_M 8  // tile order: this many pair row blocks advance together (L2 reuse)
+#endif
+constexpr int kPairStages = BM_GEMM_PAIR_STAGES;
 constexpr int kPairStageBytes = kABytes + kBBytes / 2;           // 16 KB of A + 16 KB of B: 32 KB
 constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 1024 + 256;
-constexpr int kGroupMPair = 8;     // tile order: 8 pair row blocks (2048 rows) advance together
+static_assert(kPairSmemBytes <= 232448, "shared memory per CTA");
+constexpr int kGroupMPair = BM_GEMM_PAIR_GROUP_M;
 constexpr uint32_t kPairInstrDesc = instr_desc_bf16(false, true, kBlockN, 2 * kBlockM);
 
 __device__ __forceinline__ void pair_tile_coords(const Args& a, int t, int* mb, int* nb) {

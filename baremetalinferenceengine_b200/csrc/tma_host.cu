@@ -36,14 +36,21 @@ EncodeTiled encoder() {
 // a box of box_outer rows x box_inner columns and 128-byte swizzle; reads
 // outside the tensor return zeros.
 int make_tensor_map_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
-             uint32_t box_outer, const char* what) {
+                         uint32_t box_outer, const char* what) {
+  return make_tensor_map_2d(map, base, BM_BF16, inner, outer, box_inner, box_outer, what);
+}
+
+int make_tensor_map_2d(CUtensorMap* map, const void* base, bm_dtype_t dtype, uint64_t inner, uint64_t outer,
+                       uint32_t box_inner, uint32_t box_outer, const char* what) {
   EncodeTiled enc = encoder();
   if (enc == nullptr) return fail(BM_ERR_CUDA, "%s: cuTensorMapEncodeTiled is not available", what);
+  const uint64_t es = dtype == BM_F32 ? 4 : 2;
   const cuuint64_t dims[2] = {inner, outer};
-  const cuuint64_t strides[1] = {inner * 2};
+  const cuuint64_t strides[1] = {inner * es};
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t elem[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, elem,
+  const CUtensorMapDataType type = dtype == BM_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUresult r = enc(map, type, 2, const_cast<void*>(base), dims, strides, box, elem,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(BM_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));

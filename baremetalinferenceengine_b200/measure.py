@@ -46,6 +46,7 @@ FFN_SHAPES = {
     "8b_prefill_8192": (8192, 4096, 14336),
     "8b_decode_64": (64, 4096, 14336),
     "70b_prefill_16384": (16384, 8192, 28672),
+    "70b_prefill_4096": (4096, 8192, 28672),
 }
 
 

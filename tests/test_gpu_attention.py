@@ -81,19 +81,21 @@ def test_decode_attention_matches_oracle(cuda, dt, batch, hq, hkv, hd, max_seq, 
     assert orc.worst_error(to_np(out), want) <= TOL[dt]
 
 
+@pytest.mark.parametrize("dt", ORACLE_DT, ids=["f32", "bf16"])
 @pytest.mark.parametrize("hq,hkv", [(8, 8), (16, 8), (32, 8), (64, 8), (32, 2)],
                          ids=["group1", "group2", "group4", "group8", "group16"])
 @pytest.mark.parametrize("workspace", [True, False], ids=["split", "unsplit"])
-def test_bf16_head_dim_128_tile_edges_and_stale_cache(cuda, hq, hkv, workspace):
-    """bf16 caches with head_dim 128 (the tensor-core kernel): lengths at and
-    around the 128-position tile edges, every GQA group size, and cache slots
-    past each length holding NaN, which must not reach the output."""
-    batch, hd, max_seq = 9, 128, 1024
+def test_head_dim_128_tile_edges_and_stale_cache(cuda, dt, hq, hkv, workspace):
+    """head_dim 128 (bf16: the tensor-core kernel, 128-position tiles; fp32: the
+    TMA-fed kernel, 64-position tiles): lengths at and around the tile edges,
+    every GQA group size, and cache slots past each length holding NaN, which
+    must not reach the output."""
+    batch, hd, max_seq = 12, 128, 1024
     g = gen(hq * 31 + hkv + (7 if workspace else 0))
-    q = randn((batch, hq, hd), torch.bfloat16, g)
-    kc = randn((batch, hkv, max_seq, hd), torch.bfloat16, g)
-    vc = randn((batch, hkv, max_seq, hd), torch.bfloat16, g)
-    lens = torch.tensor([1, 127, 128, 129, 255, 256, 257, 1000, 1024], dtype=torch.int32)
+    q = randn((batch, hq, hd), dt, g)
+    kc = randn((batch, hkv, max_seq, hd), dt, g)
+    vc = randn((batch, hkv, max_seq, hd), dt, g)
+    lens = torch.tensor([1, 63, 64, 65, 127, 128, 129, 255, 256, 257, 1000, 1024], dtype=torch.int32)
     for b in range(batch):  # stale slots: NaN past the length
         kc[b, :, int(lens[b]):, :] = float("nan")
         vc[b, :, int(lens[b]):, :] = float("nan")
@@ -102,7 +104,7 @@ def test_bf16_head_dim_128_tile_edges_and_stale_cache(cuda, hq, hkv, workspace):
     want, bad = oracle_attention(q, kc, vc, seq_ids, lens)
     assert bad == 0
     assert torch.isfinite(out.float()).all()
-    assert orc.worst_error(to_np(out), want) <= TOL[torch.bfloat16]
+    assert orc.worst_error(to_np(out), want) <= TOL[dt]
 
 
 def test_reference_attention_cases(cuda):
