@@ -6,8 +6,10 @@
 // One CTA per (query, kv head, split). Warp 0 streams the split's K and V rows
 // with TMA, 64 positions a tile, each row as four 128-byte-swizzled boxes of 32
 // floats, through a 3-stage ring (64 KB a stage), so that every SM keeps far more
-// bytes in flight than per-thread loads could. Warps 1-4 compute from shared
-// memory:
+// bytes in flight than per-thread loads could. Two groups of four warps compute
+// from shared memory, group h taking tiles h, h + 2, ... with its own running
+// softmax state (one group's barrier waits overlap the other's arithmetic); the
+// two states merge at the end like two splits. In each group:
 //   scores  two threads per position, 64 dimensions each (16-byte reads that the
 //           swizzle spreads over all banks), q from shared memory, one shuffle to
 //           join the halves;
@@ -15,7 +17,7 @@
 //           also makes the abort decision uniform), base-2 online update;
 //   mix     lane l owns dimensions 4l..4l+3, warp w positions w, w+4, ...;
 //           positions past the query's length are never read.
-// The four warps' accumulators are summed through shared memory at the end.
+// The warps' accumulators are summed through shared memory at the end.
 // Every mbarrier wait is bounded in time (BM_DEVERR_TIMEOUT past the limit).
 #include <cuda.h>
 
@@ -33,7 +35,8 @@ namespace {
 constexpr int kFTile = 64;                 // positions per tile
 constexpr int kFHd = 128;
 constexpr int kFStages = 3;
-constexpr int kFCompute = 128;             // compute threads (warps 1-4)
+constexpr int kFGroupThreads = 128;        // one compute group: four warps
+constexpr int kFCompute = 2 * kFGroupThreads;  // compute threads (warps 1-8)
 constexpr int kFThreads = 32 + kFCompute;
 constexpr int kFBoxBytes = kFTile * 128;   // 64 rows x 32 floats: 8 KB
 constexpr int kFHalfBytes = 4 * kFBoxBytes;  // K or V of a tile: 32 KB
@@ -41,9 +44,10 @@ constexpr int kFStageBytes = 2 * kFHalfBytes;
 constexpr int kQStride = kFHd + 4;         // q row in shared memory, the upper half 4 floats further on
 constexpr int kOffQ = kFStages * kFStageBytes;
 constexpr int kOffP = kOffQ + kMaxGroup * kQStride * 4;
-constexpr int kOffW = kOffP + kMaxGroup * kFTile * 4;  // [4][16] tile maxima
-constexpr int kOffL = kOffW + 4 * kMaxGroup * 4;       // [4][16] row sums
-constexpr int kOffBar = kOffL + 4 * kMaxGroup * 4;
+constexpr int kOffW = kOffP + 2 * kMaxGroup * kFTile * 4;  // per group: [4][16] tile maxima
+constexpr int kOffM = kOffW + 2 * 4 * kMaxGroup * 4;       // per group: [16] final running maxima
+constexpr int kOffL = kOffM + 2 * kMaxGroup * 4;           // per group: [4][16] row sums
+constexpr int kOffBar = kOffL + 2 * 4 * kMaxGroup * 4;
 constexpr int kFSmemBytes = kOffBar + (2 * kFStages + 1) * 8 + 8 + 1024;
 constexpr uint64_t kFWaitNs = 2000000000ull;
 constexpr uint64_t kFDrainNs = 200000000ull;
@@ -54,18 +58,21 @@ __device__ __forceinline__ uint32_t chunk_offset(int r, int c) {
   return static_cast<uint32_t>((c >> 3) * kFBoxBytes + r * 128 + ((((c & 7) ^ (r & 7))) << 4));
 }
 
-__device__ __forceinline__ bool compute_sync_any(bool flag) {
+// The four warps of compute group h meet at named barrier 1 + h; the result is
+// true when any of them saw `flag` set, the same for all.
+__device__ __forceinline__ bool group_sync_any(int h, bool flag) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 q, %1, 0;\n\t"
-      "bar.red.or.pred p, 1, 128, q;\n\t"
+      "setp.ne.u32 q, %2, 0;\n\t"
+      "bar.red.or.pred p, %1, 128, q;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(r)
-      : "r"(static_cast<uint32_t>(flag))
+      : "r"(1 + h), "r"(static_cast<uint32_t>(flag))
       : "memory");
   return r != 0;
 }
+__device__ __forceinline__ void group_sync(int h) { asm volatile("bar.sync %0, 128;" ::"r"(1 + h) : "memory"); }
 
 template <int GM>
 __global__ void __launch_bounds__(kFThreads, 1)
@@ -100,7 +107,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
                                                          ~static_cast<uintptr_t>(1023));
   float* q_s = reinterpret_cast<float*>(smem + kOffQ);
   float* p_s = reinterpret_cast<float*>(smem + kOffP);
-  float* wm = reinterpret_cast<float*>(smem + kOffW);
+  float* wm_all = reinterpret_cast<float*>(smem + kOffW);
+  float* mfin = reinterpret_cast<float*>(smem + kOffM);
   float* lsum = reinterpret_cast<float*>(smem + kOffL);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* empty = full + kFStages;
@@ -110,7 +118,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
   if (tid == 0) {
     for (int s = 0; s < kFStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kFCompute);
+      mbar_init(&empty[s], kFGroupThreads);  // one group consumes a tile
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -151,10 +159,12 @@ __global__ void __launch_bounds__(kFThreads, 1)
       }
     }
   } else {
-    // ---------------- compute (warps 1-4) ----------------
-    const int ct = tid - 32, cw = warp - 1;
+    // ---------------- compute (warps 1-8: two groups of four) ----------------
+    const int grp = (warp - 1) >> 2, cw = (warp - 1) & 3, ct = (tid - 32) & (kFGroupThreads - 1);
     const int pos = ct >> 1, half = ct & 1;  // scores: position pos, dims [64 half, 64 half + 64)
     const float* qh = q_s + half * (64 + 4);
+    float* wm = wm_all + grp * 4 * kMaxGroup;
+    float* p_g = p_s + grp * kMaxGroup * kFTile;
 #pragma unroll
     for (int g = 0; g < GM; ++g) {
       m_run[g] = -INFINITY;
@@ -162,7 +172,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[g][e] = 0.f;
     }
-    for (int i = 0; i < n_tiles; ++i) {
+    for (int i = grp; i < n_tiles; i += 2) {
       const int s = i % kFStages;
       int ok = 1;
       if (lane == 0) {
@@ -203,7 +213,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
         for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
         if (lane == 0) wm[cw * kMaxGroup + g] = v;
       }
-      if (compute_sync_any(*abort_flag != 0)) break;
+      if (group_sync_any(grp, *abort_flag != 0)) break;
 #pragma unroll
       for (int g = 0; g < GM; ++g) {
         if (g < G) {
@@ -214,19 +224,19 @@ __global__ void __launch_bounds__(kFThreads, 1)
           m_run[g] = m_new;
           const float p = valid ? exp2f(sc[g] - m_new) : 0.f;
           l_part[g] = l_part[g] * alpha + (half == 0 ? p : 0.f);
-          if (half == 0) p_s[g * kFTile + pos] = p;
+          if (half == 0) p_g[g * kFTile + pos] = p;
 #pragma unroll
           for (int e = 0; e < 4; ++e) acc[g][e] *= alpha;
         }
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");  // P of this tile is written
+      group_sync(grp);  // P of this tile is written
       // mix: lane owns dims 4 lane .. 4 lane + 3; rows past the length are not read
       for (int j = cw; j < tile_valid; j += 4) {
         const float4 vv = *reinterpret_cast<const float4*>(vt + chunk_offset(j, lane));
 #pragma unroll
         for (int g = 0; g < GM; ++g) {
           if (g < G) {
-            const float p = p_s[g * kFTile + j];
+            const float p = p_g[g * kFTile + j];
             acc[g][0] = fmaf(p, vv.x, acc[g][0]);
             acc[g][1] = fmaf(p, vv.y, acc[g][1]);
             acc[g][2] = fmaf(p, vv.z, acc[g][2]);
@@ -235,23 +245,23 @@ __global__ void __launch_bounds__(kFThreads, 1)
         }
       }
       mbar_arrive(&empty[s]);  // this thread is done with the stage
-      asm volatile("bar.sync 1, 128;" ::: "memory");  // p_s and wm may be rewritten by the next tile
+      group_sync(grp);  // P and the maxima may be rewritten by the group's next tile
     }
     // row sums (each half-0 thread holds its positions' share) and the running maxima
 #pragma unroll
     for (int g = 0; g < GM; ++g) {
       const float v = warp_sum(l_part[g]);
-      if (lane == 0) lsum[cw * kMaxGroup + g] = v;
+      if (lane == 0) lsum[(grp * 4 + cw) * kMaxGroup + g] = v;
     }
     if (ct == 0) {
 #pragma unroll
-      for (int g = 0; g < GM; ++g) wm[g] = m_run[g];  // the same in every compute thread
+      for (int g = 0; g < GM; ++g) mfin[grp * kMaxGroup + g] = m_run[g];  // the same in every thread of the group
     }
   }
   __syncthreads();  // the producer has drained its copies: stage 0 is free for the reduction
-  float* red = reinterpret_cast<float*>(smem);  // [4][GM][128]
+  float* red = reinterpret_cast<float*>(smem);  // [2 groups x 4 warps][GM][128]: at most 64 KB, stage 0
   if (warp >= 1) {
-    const int cw = warp - 1;
+    const int cw = warp - 1;  // group * 4 + warp of the group
 #pragma unroll
     for (int g = 0; g < GM; ++g) {
       *reinterpret_cast<float4*>(red + (cw * GM + g) * kFHd + lane * 4) =
@@ -262,17 +272,27 @@ __global__ void __launch_bounds__(kFThreads, 1)
   if (warp >= 1) {
     for (int i = tid - 32; i < G * kFHd; i += kFCompute) {
       const int g = i / kFHd, d = i - g * kFHd;
-      float o = 0.f;
+      // merge the two groups' (max, sum, output) like two splits
+      const float m0 = mfin[g], m1 = mfin[kMaxGroup + g];
+      const float m = fmaxf(m0, m1);  // finite: group 0 holds at least one tile
+      const float f0 = exp2f(m0 - m), f1 = m1 == -INFINITY ? 0.f : exp2f(m1 - m);
+      float o0 = 0.f, o1 = 0.f, l0 = 0.f, l1 = 0.f;
 #pragma unroll
-      for (int w = 0; w < 4; ++w) o += red[(w * GM + g) * kFHd + d];
-      const float l = lsum[g] + lsum[kMaxGroup + g] + lsum[2 * kMaxGroup + g] + lsum[3 * kMaxGroup + g];
+      for (int w = 0; w < 4; ++w) {
+        o0 += red[(w * GM + g) * kFHd + d];
+        o1 += red[((4 + w) * GM + g) * kFHd + d];
+        l0 += lsum[w * kMaxGroup + g];
+        l1 += lsum[(4 + w) * kMaxGroup + g];
+      }
+      const float o = o0 * f0 + o1 * f1;
+      const float l = l0 * f0 + l1 * f1;
       if (ws == nullptr) {
         float* out = static_cast<float*>(a.out) + (b * a.hq + static_cast<int64_t>(kvh) * G + g) * kFHd;
         out[d] = o / l;
       } else {
         ws[g * (kFHd + 2) + d] = o;
         if (d == 0) {
-          ws[g * (kFHd + 2) + kFHd] = wm[g];
+          ws[g * (kFHd + 2) + kFHd] = m;
           ws[g * (kFHd + 2) + kFHd + 1] = l;
         }
       }
