@@ -59,7 +59,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama70b_bf16")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(OP_ROWS), default="llama70b_bf16",
+                    help="a layer-step workload (default) or one of the tensor-core op rows")
     ap.add_argument("--rows", type=int, default=0, help="override tokens per GPU")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--e2e-chunks", type=int, default=16)
@@ -311,12 +312,292 @@ def config_dict(shape, n):
             "parallelism": f"rows{n}: tokens partitioned across {n} GPU(s), no collectives"}
 
 
+# ----------------------------------------------------------------------------- op rows
+# The two contractions beyond the layer-op path, each as its own bench line with
+# the same contract: decode attention over a resident KV cache, and the FFN
+# front half (two projections + SwiGLU). A step is one call over one batch.
+
+OP_ROWS = {
+    "attention_8b_decode_b64_bf16": dict(kind="attention", batch=64, hq=32, hkv=8, hd=128, max_seq=8192,
+                                         dtype="bf16", description="Llama-3-8B decode attention: 64 queries, "
+                                         "32 Q / 8 KV heads of 128, 8192 cached positions each"),
+    "attention_8b_decode_b64_f32": dict(kind="attention", batch=64, hq=32, hkv=8, hd=128, max_seq=8192,
+                                        dtype="f32", description="the same in fp32"),
+    "attention_70b_decode_b64_bf16": dict(kind="attention", batch=64, hq=64, hkv=8, hd=128, max_seq=8192,
+                                          dtype="bf16", description="Llama-3-70B decode attention: 64 queries, "
+                                          "64 Q / 8 KV heads of 128, 8192 cached positions each"),
+    "ffn_gemm_swiglu_8b_prefill_bf16": dict(kind="ffn", rows=32768, dim=4096, hidden=14336, dtype="bf16",
+                                            description="Llama-3-8B FFN front half over 32768 prefill tokens: "
+                                            "silu(x Wg) * (x Wu), dim 4096, hidden 14336"),
+    "ffn_gemm_swiglu_70b_prefill_bf16": dict(kind="ffn", rows=16384, dim=8192, hidden=28672, dtype="bf16",
+                                             description="Llama-3-70B FFN front half over 16384 prefill tokens"),
+}
+OP_METRIC = {"attention": ("decode attention: algorithmic HBM GB/s of K/V read", "GB/s"),
+             "ffn": ("fused GEMM + SwiGLU: TFLOP/s", "TFLOP/s")}
+
+
+def measured_bf16_peak():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, 1400.0, "fallback"
+
+
+class OpRow:
+    """Device inputs of one op row and its call through the public API."""
+
+    def __init__(self, spec, dev, seed):
+        import ctypes
+
+        import torch
+
+        from baremetalinferenceengine_b200 import _lib, ops
+        self.spec, self.dev = spec, dev
+        self.dt = torch.bfloat16 if spec["dtype"] == "bf16" else torch.float32
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        self.status = ops.DeviceStatus(dev)
+        if spec["kind"] == "attention":
+            b, hq, hkv, hd, S = spec["batch"], spec["hq"], spec["hkv"], spec["hd"], spec["max_seq"]
+            self.kc = torch.randn(b, hkv, S, hd, device=dev, generator=g).to(self.dt)
+            self.vc = torch.randn(b, hkv, S, hd, device=dev, generator=g).to(self.dt)
+            self.q = torch.randn(b, hq, hd, device=dev, generator=g).to(self.dt)
+            self.out = torch.empty_like(self.q)
+            self.lens = torch.full((b,), S, dtype=torch.int32, device=dev)
+            self.seq = torch.arange(b, dtype=torch.int32, device=dev)
+            L = _lib.load()
+            need = ctypes.c_size_t()
+            _lib.check(L.bm_decode_attention_workspace_size(b, hq, hkv, hd, S, ctypes.byref(need)))
+            self.need = need.value
+            self.ws = torch.empty(max(1, need.value), dtype=torch.uint8, device=dev)
+            es = self.q.element_size()
+            self.bytes = b * S * hkv * hd * es * 2 + 2 * self.q.numel() * es
+            self.units = self.bytes / 1e9  # GB per step
+            self.launches = 1 + (1 if need.value > 0 else 0)
+            self.inputs, self.outputs = [self.q], [self.out]
+        else:
+            r, d, h = spec["rows"], spec["dim"], spec["hidden"]
+            self.x = torch.randn(r, d, device=dev, generator=g).to(self.dt)
+            self.wg = (torch.randn(d, h, device=dev, generator=g) * 0.02).to(self.dt)
+            self.wu = (torch.randn(d, h, device=dev, generator=g) * 0.02).to(self.dt)
+            self.out = torch.empty(r, h, device=dev, dtype=self.dt)
+            self.flops = 4.0 * r * d * h
+            self.units = self.flops / 1e12  # TFLOP per step
+            self.launches = 1
+            self.inputs, self.outputs = [self.x], [self.out]
+
+    def call(self, stream):
+        import torch
+
+        from baremetalinferenceengine_b200 import _lib, ops
+        sp = self.spec
+        if sp["kind"] == "attention":
+            L = _lib.load()
+            _lib.check(L.bm_decode_attention(
+                self.out.data_ptr(), self.q.data_ptr(), self.kc.data_ptr(), self.vc.data_ptr(), self.seq.data_ptr(),
+                self.lens.data_ptr(), sp["max_seq"], sp["batch"], sp["hq"], sp["hkv"], sp["hd"], sp["max_seq"],
+                sp["batch"], 0.0, self.ws.data_ptr(), self.need, ops.bm_dtype(self.q), self.status.ptr,
+                stream.cuda_stream))
+        else:
+            with torch.cuda.stream(stream):
+                ops.gemm_swiglu(self.x, self.wg, self.wu, out=self.out, status=self.status, stream=stream)
+
+
+def cpu_op_row(spec, threads: int, target_s: float, reps: int = 0, warmup: int = 0):
+    """The oracle on a bounded sample: one call per host thread (a query's
+    attention, or one row of the FFN), repeated to about target_s (or exactly
+    `reps` times after `warmup`). Returns (value in the row's unit, sample
+    description, wall seconds per repetition)."""
+    import numpy as np
+
+    from oracle import oracle as orc
+    rng = np.random.default_rng(7)
+    bf16 = spec["dtype"] == "bf16"
+
+    def host(shape, scale=1.0):
+        x = (rng.standard_normal(shape, dtype=np.float32) * scale)
+        return orc.f32_to_bf16(x) if bf16 else x
+
+    if spec["kind"] == "attention":
+        hq, hkv, hd, S = spec["hq"], spec["hkv"], spec["hd"], spec["max_seq"]
+        per = [(host((1, hq, hd)), host((1, hkv, S, hd)), host((1, hkv, S, hd)), np.zeros((1, hq, hd),
+                np.uint16 if bf16 else np.float32)) for _ in range(threads)]
+        lens = np.full(1, S, np.int32)
+        L = orc.lib()
+
+        def job(i):
+            q, k, v, o = per[i]
+            return lambda: L.oracle_decode_attention(o.ctypes.data, q.ctypes.data, k.ctypes.data, v.ctypes.data,
+                                                     None, lens.ctypes.data, 1, hq, hkv, hd, S, 1, 0 if not bf16 else 1)
+        jobs = [job(i) for i in range(threads)]
+        unit_per_rep = threads * (S * hkv * hd * (2 if bf16 else 4) * 2) / 1e9
+        sample = f"{threads} of {spec['batch']} queries (full 8192-position caches), oracle_decode_attention, one per thread"
+    else:
+        d, h = spec["dim"], spec["hidden"]
+        wg, wu = host((d, h), 0.02), host((d, h), 0.02)
+        xs = [host((1, d)) for _ in range(threads)]
+        outs = [np.zeros((1, h), wg.dtype) for _ in range(threads)]
+        L = orc.lib()
+
+        def job(i):
+            return lambda: L.oracle_gemm_swiglu(outs[i].ctypes.data, xs[i].ctypes.data, wg.ctypes.data,
+                                                wu.ctypes.data, 1, d, h, 1 if bf16 else 0, 1)
+        jobs = [job(i) for i in range(threads)]
+        unit_per_rep = threads * 4.0 * d * h / 1e12
+        sample = f"{threads} of {spec['rows']} rows, oracle_gemm_swiglu, one row per thread"
+    def once():
+        ths = [threading.Thread(target=j) for j in jobs]
+        t0 = time.perf_counter()
+        for t in ths:
+            t.start()
+        for t in ths:
+            t.join()
+        return time.perf_counter() - t0
+
+    for _ in range(warmup):
+        once()
+    times = []
+    while (len(times) < reps) if reps else (not times or (sum(times) < target_s and len(times) < 20)):
+        times.append(once())
+    return unit_per_rep / statistics.median(times), sample, times
+
+
+def op_row_config(name, spec, n):
+    c = {"workload": name, "description": spec["description"], "parallelism":
+         f"rows{n}: each GPU its own instance (weak scaling), no collectives",
+         "l2": "inputs larger than L2 (> 1 GB per step): no flush needed"}
+    c.update({k: v for k, v in spec.items() if k not in ("description",)})
+    return c
+
+
+def run_op_row(args) -> int:
+    spec = OP_ROWS[args.workload]
+    metric, unit = OP_METRIC[spec["kind"]]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    K, W = args.steps, args.warmup
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        threads = host_threads()
+        value, sample, times = cpu_op_row(spec, threads, 0.0, reps=K, warmup=W)
+        value = sum(times) and (value * statistics.median(times) * len(times) / sum(times))  # K steps / total time
+        line = {"metric": metric, "value": round(value, 4), "unit": unit, "n_gpus": args.gpus, "steps": K,
+                "warmup": W, "ms_per_step": round(sum(times) / K * 1e3, 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": spec["dtype"], "data": "synthetic (seeded N(0,1))",
+                "impl": "reference", "config": op_row_config(args.workload, spec, args.gpus),
+                "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": threads, "kind": "port",
+                                 "sample": sample},
+                "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return 0
+
+    import torch
+    import torch.distributed as dist
+
+    from baremetalinferenceengine_b200 import shard
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        log(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 under torchrun")
+        return 2
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    row = OpRow(spec, dev, seed=2000 + rank)
+    stream = torch.cuda.Stream(dev)
+    for _ in range(W):
+        row.call(stream)
+    stream.synchronize()
+    assert row.status.read(stream) == 0, "device status set during warm-up"
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(dev) as clocks:
+        for i in range(K):
+            ev[i][0].record(stream)
+            row.call(stream)
+            ev[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    assert row.status.read(stream) == 0, "device status set during the timed steps"
+    per_step = [e0.elapsed_time(e1) for e0, e1 in ev]
+    elapsed_ms = shard.max_over_ranks([sum(per_step)], device=dev)[0]
+    value = world * row.units * K / (elapsed_ms / 1e3)
+    mean_ms = elapsed_ms / K
+    if spec["kind"] == "attention":
+        peak, kind = measured_peak()
+        achieved = row.bytes / (mean_ms / 1e3) / 1e9
+        roofline = {"kernel": "bm_decode_attention", "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                    "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                    "peak_source": f"{kind} hbm_gbs", "algorithmic_bytes_per_launch": row.bytes}
+    else:
+        burst, sustained, kind = measured_bf16_peak()
+        achieved = row.flops / (mean_ms / 1e3) / 1e12
+        roofline = {"kernel": "bm_gemm_swiglu", "bound": "tensor", "achieved": round(achieved, 1), "peak": burst,
+                    "unit": "TFLOP/s", "frac": round(achieved / burst, 4), "frac_of_sustained":
+                    round(achieved / sustained, 4), "traffic": None, "peak_source": f"{kind} bf16_tflops (burst)",
+                    "algorithmic_flops_per_launch": row.flops}
+    line = {"metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": round(mean_ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": spec["dtype"], "data": "synthetic: seeded N(0,1) caches / activations, N(0,0.02) weights",
+            "impl": "ours", "config": op_row_config(args.workload, spec, world), "roofline": roofline,
+            "gpu_launches": row.launches * K, "clocks": clocks.summary() if rank == 0 else None}
+    if not args.no_e2e:
+        # the resident state (cache or weights) stays on the device; each step's
+        # inputs come from pinned host memory and its output goes back
+        h_in = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in row.inputs]
+        h_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in row.outputs]
+        for h, t in zip(h_in, row.inputs):
+            h.copy_(t)
+        E = max(1, args.e2e_steps)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(E):
+                for h, t in zip(h_in, row.inputs):
+                    t.copy_(h, non_blocking=True)
+                row.call(stream)
+                for h, t in zip(h_out, row.outputs):
+                    h.copy_(t, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        e2e_ms = shard.max_over_ranks([e0.elapsed_time(e1)], device=dev)[0]
+        line["e2e"] = {"value": round(world * row.units * E / (e2e_ms / 1e3), 2), "unit": unit,
+                       "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in row.inputs),
+                       "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in row.outputs),
+                       "steps": E, "how": "per step: pinned-host -> device copy of the inputs, the call, device -> "
+                       "pinned-host copy of the output; the KV cache or the weights stay resident"}
+    if world == 1 and not args.no_cpu_baseline:
+        threads = host_threads()
+        cv, sample, times = cpu_op_row(spec, threads, args.cpu_seconds)
+        line["cpu_baseline"] = {"value": round(cv, 4), "unit": unit, "cores": threads, "kind": "port",
+                                "sample": f"{sample}, {len(times)} repetitions, median taken"}
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 # ----------------------------------------------------------------------------- main (ours)
 
 def main() -> int:
     args = parse_args()
     from baremetalinferenceengine_b200.layer import WORKLOADS
 
+    if args.workload in OP_ROWS:
+        return run_op_row(args)
     shape = WORKLOADS[args.workload]
     if args.rows:
         shape = shape.with_rows(args.rows)
