@@ -123,14 +123,15 @@ __global__ void __launch_bounds__(kFThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
+  __syncthreads();  // barriers exist: the first copies start while the queries are staged
   if (warp >= 1) {  // the group's queries, each row's upper half 4 floats further on (no bank clash)
     const float* qb = static_cast<const float*>(a.q) + (b * a.hq + static_cast<int64_t>(kvh) * G) * kFHd;
     for (int i = tid - 32; i < G * kFHd; i += kFCompute) {
       const int g = i / kFHd, d = i - g * kFHd;
       q_s[g * kQStride + d + (d >= 64 ? 4 : 0)] = __ldg(qb + i);
     }
+    asm volatile("bar.sync 3, 256;" ::: "memory");  // every compute thread reads all of q_s
   }
-  __syncthreads();
 
   float m_run[GM], l_part[GM], acc[GM][4];  // compute threads: running max, sum share, accumulator
   if (warp == 0) {
@@ -316,8 +317,7 @@ int launch_f32_tma(const AttnArgs& a, cudaStream_t stream) {
   if (int st = make_tensor_map_2d(&tv, a.v_cache, BM_F32, kFHd, rows, 32, kFTile, what)) return st;
   const dim3 grid(a.splits, a.hkv, static_cast<unsigned>(a.batch));
   auto go = [&](auto kernel) {
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFSmemBytes);
-    if (err != cudaSuccess) return fail(BM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+    if (int st = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), kFSmemBytes, what)) return st;
     kernel<<<grid, kFThreads, kFSmemBytes, stream>>>(tk, tv, a);
     return check_launch(what);
   };

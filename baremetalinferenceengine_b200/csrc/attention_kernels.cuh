@@ -350,8 +350,9 @@ int launch_group(const AttnArgs& a, size_t smem, cudaStream_t stream) {
   const dim3 grid(a.splits, a.hkv, static_cast<unsigned>(a.batch));
   auto go = [&](auto kernel) {
     if (smem > 48 * 1024) {
-      cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-      if (err != cudaSuccess) return fail(BM_ERR_CUDA, "bm_decode_attention: %s", cudaGetErrorString(err));
+      if (int st = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), static_cast<int>(smem), "bm_decode_attention")) {
+        return st;
+      }
     }
     kernel<<<grid, kThreads, smem, stream>>>(a);
     return check_launch("bm_decode_attention");

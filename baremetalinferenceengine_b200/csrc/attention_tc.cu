@@ -52,7 +52,7 @@ constexpr int kOffP = kOffQ + kQBytes;                 // two P buffers
 constexpr int kOffMax = kOffP + 2 * kPBytes;           // [2][4][16] floats
 constexpr int kOffL = kOffMax + 2 * 4 * kTcN * 4;      // [4][16] floats
 constexpr int kOffBar = kOffL + 4 * kTcN * 4;
-constexpr int kNumBars = 2 * kTcStages + 5 * 2 + 1;
+constexpr int kNumBars = 2 * kTcStages + 5 * 2 + 2;
 constexpr int kTcSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024 /* alignment slack */;
 constexpr uint32_t kTmemCols = 64;
 constexpr uint64_t kWaitNs = 2000000000ull;
@@ -135,7 +135,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* ofull = pfull + 2;          // mix MMA done            (commit)
   uint64_t* ofree = ofull + 2;          // mix output read         (128)
   uint64_t* mma_done = ofree + 2;
-  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* q_ready = mma_done + 1;     // queries and zeroed P in shared memory (128)
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(q_ready + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_s + 1);
 
   if (tid == 0) {
@@ -151,10 +152,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&ofree[i], kTcSoftmaxThreads);
     }
     mbar_init(mma_done, 1);
+    mbar_init(q_ready, kTcSoftmaxThreads);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_base_s, kTmemCols);
+  tc_fence_before();
+  __syncthreads();  // barriers and TMEM exist: the first copies start while the queries are staged
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_s;
   if (warp >= 2) {
     // the group's queries, rows >= G zero, as the score MMA's K-major B operand
     const int t = tid - 64;
@@ -169,11 +175,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       *reinterpret_cast<uint4*>(p_s + c * 16) = make_uint4(0u, 0u, 0u, 0u);
     }
     fence_proxy_async_smem();
+    mbar_arrive(q_ready);
   }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_base_s;
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
@@ -201,7 +204,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---------------- MMA issuer ----------------
     bool issued = false;
     const uint32_t q_addr = smem_u32(q_s);
-    for (int i = 0; i <= n_tiles; ++i) {
+    const bool q_ok = wait_phase(q_ready, 0, abort_flag, a.status, kWaitNs, true);
+    for (int i = 0; q_ok && i <= n_tiles; ++i) {
       if (i < n_tiles) {  // scores of tile i
         const int s = i % kTcStages;
         if (!wait_phase(&full[s], static_cast<uint32_t>((i / kTcStages) & 1), abort_flag, a.status, kWaitNs, true)) {
@@ -379,8 +383,7 @@ int launch_tc(const AttnArgs& a, cudaStream_t stream) {
   if (int st = make_tensor_map_bf16(&tv, a.v_cache, kTcHd, rows, 64, kTcTile, what)) return st;
   const dim3 grid(a.splits, a.hkv, static_cast<unsigned>(a.batch));
   auto go = [&](auto kernel) {
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes);
-    if (err != cudaSuccess) return fail(BM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+    if (int st = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), kTcSmemBytes, what)) return st;
     kernel<<<grid, kTcThreads, kTcSmemBytes, stream>>>(tk, tv, a);
     return check_launch(what);
   };

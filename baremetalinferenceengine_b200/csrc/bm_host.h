@@ -21,6 +21,10 @@ int check_launch(const char* what);
 // Streaming multiprocessors of the current device (cached per device).
 int sm_count();
 
+// cudaFuncSetAttribute(kernel, MaxDynamicSharedMemorySize, bytes) on the current
+// device, once per (device, kernel): later calls cost a lookup, not a driver call.
+int allow_dynamic_smem(const void* kernel, int bytes, const char* what);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 inline int dtype_size(bm_dtype_t dt) { return dt == BM_F32 ? 4 : 2; }

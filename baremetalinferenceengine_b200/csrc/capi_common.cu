@@ -3,6 +3,10 @@
 #include <cstdarg>
 #include <cstdio>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "bm_host.h"
 
 namespace bm {
@@ -39,6 +43,20 @@ int sm_count() {
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
   if (dev < kMaxDevices) g_sm_count[dev] = n;
   return n;
+}
+
+int allow_dynamic_smem(const void* kernel, int bytes, const char* what) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> granted;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = granted.find({dev, kernel});
+  if (it != granted.end() && it->second >= bytes) return BM_OK;
+  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (err != cudaSuccess) return fail(BM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+  granted[{dev, kernel}] = bytes;
+  return BM_OK;
 }
 
 }  // namespace bm

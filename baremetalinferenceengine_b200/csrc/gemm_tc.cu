@@ -545,15 +545,13 @@ int run(const char* what, void* out, const void* x, const void* w0, const void* 
   if (paired) {
     const int grid = 2 * static_cast<int>(std::min<int64_t>(tiles, sm_count() / 2));
     auto kernel = gemm_tc_pair_kernel<SWIGLU>;
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes);
-    if (err != cudaSuccess) return fail(BM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+    if (int st = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), kPairSmemBytes, what)) return st;
     kernel<<<grid, kThreads, kPairSmemBytes, as_stream(stream)>>>(ta, tb0, tb1, a);
     return check_launch(what);
   }
   const int grid = static_cast<int>(std::min<int64_t>(tiles, sm_count()));
   auto kernel = gemm_tc_kernel<SWIGLU>;
-  cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  if (err != cudaSuccess) return fail(BM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+  if (int st = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), kSmemBytes, what)) return st;
   kernel<<<grid, kThreads, kSmemBytes, as_stream(stream)>>>(ta, tb0, tb1, a);
   return check_launch(what);
 }

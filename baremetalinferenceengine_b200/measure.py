@@ -4,10 +4,11 @@
     python -m baremetalinferenceengine_b200.measure ffn       [--shapes a,b] [--reps 10] [--once]
 
 One JSON line per shape on stdout. Inputs are seeded synthetic tensors of the
-Llama-3 8B / 70B decode and prefill shapes, resident on the GPU; each timed call
-is preceded by a 256 MB write that evicts L2 and timed alone with CUDA events on
-its stream (median of --reps). ``--once`` makes two untimed calls per shape and
-nothing else (for profilers).
+Llama-3 8B / 70B decode and prefill shapes, resident on the GPU. The call is
+captured once in a CUDA graph (so the timed window holds GPU work only, not the
+host's launch path); each replay is preceded by a 256 MB write that evicts L2
+and timed alone with CUDA events on its stream (median of --reps). ``--once``
+makes two untimed calls per shape and nothing else (for profilers).
 
 attention: algorithmic bytes = the K and V rows every query reads plus q and the
     output; roofline = HBM (hbm_gbs of MEASURED_PEAKS.json, else 6650 GB/s).
@@ -61,17 +62,23 @@ def peaks():
 
 
 def time_call(fn, reps: int, dev) -> float:
-    """Median milliseconds of fn() over reps calls, each after an L2-evicting write."""
+    """Median milliseconds of one replay of fn() captured as a CUDA graph, over
+    reps replays, each after an L2-evicting write."""
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     for _ in range(3):
         fn()
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=torch.cuda.Stream(dev)):
+        fn()
+    graph.replay()
     torch.cuda.synchronize(dev)
     times = []
     for _ in range(reps):
         flush.zero_()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        fn()
+        graph.replay()
         e1.record()
         e1.synchronize()
         times.append(e0.elapsed_time(e1))
@@ -98,13 +105,12 @@ def attention(names, reps: int, once: bool, dev) -> None:
         _lib.check(L.bm_decode_attention_workspace_size(batch, hq, hkv, hd, max_seq, ctypes.byref(need)))
         ws = torch.empty(max(1, need.value), dtype=torch.uint8, device=dev)
         status = ops.DeviceStatus(dev)
-        stream = torch.cuda.current_stream(dev).cuda_stream
 
         def call():
             _lib.check(L.bm_decode_attention(out.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(),
                                              seq_ids.data_ptr(), lens.data_ptr(), max_seq, batch, hq, hkv, hd,
                                              max_seq, batch, 0.0, ws.data_ptr(), need.value, ops.bm_dtype(q),
-                                             status.ptr, stream))
+                                             status.ptr, torch.cuda.current_stream(dev).cuda_stream))
 
         if once:
             call()
@@ -123,7 +129,7 @@ def attention(names, reps: int, once: bool, dev) -> None:
             "kernel": "tcgen05" if es == 2 and hd == 128 else "cuda cores",
             "ms": round(ms, 4), "algorithmic_bytes": nbytes, "gbs": round(gbs, 1),
             "roofline": {"bound": "hbm", "peak": hbm, "peak_source": hbm_src, "frac": round(gbs / hbm, 4)},
-            "l2": "flushed before each call"}), flush=True)
+            "l2": "flushed before each call", "timing": "CUDA-graph replay"}), flush=True)
         del kc, vc
         torch.cuda.empty_cache()
 
@@ -163,7 +169,7 @@ def ffn(names, reps: int, once: bool, dev) -> None:
                          "frac": round(tflops / tf_peak, 4)},
             "cublas_matmul_plus_swiglu_ms": round(cublas_ms, 4),
             "cublas_tflops": round(flops / (cublas_ms / 1e3) / 1e12, 1),
-            "l2": "flushed before each call"}), flush=True)
+            "l2": "flushed before each call", "timing": "CUDA-graph replay"}), flush=True)
         del x, wg, wu, out
         torch.cuda.empty_cache()
 
