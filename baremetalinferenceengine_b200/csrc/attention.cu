@@ -27,6 +27,12 @@
 namespace bm {
 namespace attn {
 
+#ifndef BM_ATTN_STAGED_MIN_TILES
+#define BM_ATTN_STAGED_MIN_TILES 4
+#endif
+// Splits of the TMA-fed kernels hold at least this many 128-position tiles.
+constexpr int kStagedMinTiles = BM_ATTN_STAGED_MIN_TILES;
+
 // min_tiles: the fewest tiles a split may hold (the tensor-core kernel pays a
 // fixed start-up per CTA, so its splits keep at least four tiles).
 void plan_splits(int64_t pairs, int max_len, int sms, int* splits, int* split_len, int min_tiles = 1) {
@@ -97,7 +103,7 @@ int decode_attention(void* out, const void* q, const void* k_cache, const void* 
   a.status = d_status;
   const bool tc = tc_eligible(a, dtype);
   plan_splits(batch * hkv, max_len, sm_count(), &a.splits, &a.split_len,
-              tc || f32_tma_eligible(a, dtype) ? 4 : 1);
+              tc || f32_tma_eligible(a, dtype) ? kStagedMinTiles : 1);
   const size_t need = workspace_bytes(batch, hkv, a.group, hd, a.splits);
   if (need > 0 && (workspace == nullptr || workspace_size < need)) {
     // Less scratch than the plan wants: as many splits as it holds (maybe one).

@@ -334,8 +334,7 @@ int launch_f32_tma(const AttnArgs& a, cudaStream_t stream) {
     st = go(attention_f32_tma_kernel<16>);
   }
   if (st != BM_OK || a.splits == 1) return st;
-  attention_combine_kernel<float><<<dim3(a.hq, static_cast<unsigned>(a.batch)), std::min(256, a.hd), 0, stream>>>(a);
-  return check_launch("bm_decode_attention (combine)");
+  return launch_combine<float>(a, stream);
 }
 
 }  // namespace attn

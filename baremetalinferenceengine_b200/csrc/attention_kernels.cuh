@@ -313,33 +313,72 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(AttnArgs a) {
   }
 }
 
-// One CTA per (query, q head): merges the splits' (max, sum, output) partials.
+// One CTA of kCombineThreads per (query, q head): merges the splits' (max, sum,
+// output) partials. The splits' maxima and sums are read in parallel and turned
+// into per-split weights in shared memory (dynamic, one float per split), so each
+// output dimension is one pass of independent loads over the splits.
+constexpr int kCombineThreads = 128;
+
+template <int NW>
+__device__ __forceinline__ float combine_block_reduce(float v, bool is_max, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float o = __shfl_xor_sync(0xffffffffu, v, off);
+    v = is_max ? fmaxf(v, o) : v + o;
+  }
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  v = red[0];
+#pragma unroll
+  for (int w = 1; w < NW; ++w) v = is_max ? fmaxf(v, red[w]) : v + red[w];
+  __syncthreads();
+  return v;
+}
+
 template <typename T>
-__global__ void __launch_bounds__(256) attention_combine_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kCombineThreads) attention_combine_kernel(AttnArgs a) {
+  extern __shared__ float w_s[];  // [splits]
+  __shared__ float red[kCombineThreads / 32];
   const int64_t b = blockIdx.y;
   const int h = blockIdx.x;
   int seq, len;
   if (check_query(a, b, &seq, &len)) return;  // reported by the split kernel
   const int kvh = h / a.group, g = h - kvh * a.group;
-  const int hd = a.hd;
+  const int hd = a.hd, tid = threadIdx.x;
   const float* base = a.ws + ((b * a.hkv + kvh) * a.splits * a.group + g) * static_cast<int64_t>(hd + 2);
   const int64_t split_stride = static_cast<int64_t>(a.group) * (hd + 2);
   float m = -INFINITY;
-  for (int s = 0; s < a.splits; ++s) m = fmaxf(m, base[s * split_stride + hd]);
+  for (int s = tid; s < a.splits; s += kCombineThreads) m = fmaxf(m, base[s * split_stride + hd]);
+  m = combine_block_reduce<kCombineThreads / 32>(m, true, red);  // finite: split 0 is never empty
   float l = 0.f;
-  for (int s = 0; s < a.splits; ++s) {
+  for (int s = tid; s < a.splits; s += kCombineThreads) {
     const float ms = base[s * split_stride + hd];
-    if (ms != -INFINITY) l += base[s * split_stride + hd + 1] * exp2f(ms - m);
+    const float w = ms == -INFINITY ? 0.f : exp2f(ms - m);
+    w_s[s] = w;
+    l += base[s * split_stride + hd + 1] * w;
   }
+  l = combine_block_reduce<kCombineThreads / 32>(l, false, red);  // its barriers also publish w_s
   T* out = static_cast<T*>(a.out) + (b * a.hq + h) * hd;
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+  for (int d = tid; d < hd; d += kCombineThreads) {
     float o = 0.f;
+#pragma unroll 4
     for (int s = 0; s < a.splits; ++s) {
-      const float ms = base[s * split_stride + hd];
-      if (ms != -INFINITY) o += base[s * split_stride + d] * exp2f(ms - m);
+      // an empty split writes only its maximum and sum: its output slots hold
+      // whatever the workspace held before, so they are skipped, not weighted by 0
+      const float w = w_s[s];
+      if (w != 0.f) o = fmaf(base[s * split_stride + d], w, o);
     }
     store1<T>(out + d, o / l);
   }
+}
+
+// Launches the combine step for a split plan.
+template <typename T>
+int launch_combine(const AttnArgs& a, cudaStream_t stream) {
+  attention_combine_kernel<T><<<dim3(a.hq, static_cast<unsigned>(a.batch)), kCombineThreads,
+                                static_cast<size_t>(a.splits) * sizeof(float), stream>>>(a);
+  return check_launch("bm_decode_attention (combine)");
 }
 
 // Splits for `pairs` (query, kv head) pairs over at most max_len positions:
@@ -390,8 +429,7 @@ int launch(AttnArgs a, cudaStream_t stream) {
     st = launch_group<T, 16>(a, smem, stream);
   }
   if (st != BM_OK || a.splits == 1) return st;
-  attention_combine_kernel<T><<<dim3(a.hq, static_cast<unsigned>(a.batch)), std::min(256, a.hd), 0, stream>>>(a);
-  return check_launch("bm_decode_attention (combine)");
+  return launch_combine<T>(a, stream);
 }
 
 

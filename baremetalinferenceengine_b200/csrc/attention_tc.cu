@@ -401,8 +401,7 @@ int launch_tc(const AttnArgs& a, cudaStream_t stream) {
   }
   if (st != BM_OK) return st;
   if (a.splits == 1) return BM_OK;
-  attention_combine_kernel<bf16><<<dim3(a.hq, static_cast<unsigned>(a.batch)), std::min(256, a.hd), 0, stream>>>(a);
-  return check_launch("bm_decode_attention (combine)");
+  return launch_combine<bf16>(a, stream);
 }
 
 }  // namespace attn

@@ -107,6 +107,35 @@ def test_head_dim_128_tile_edges_and_stale_cache(cuda, dt, hq, hkv, workspace):
     assert orc.worst_error(to_np(out), want) <= TOL[dt]
 
 
+@pytest.mark.parametrize("dt", ORACLE_DT, ids=["f32", "bf16"])
+def test_stale_workspace_contents_do_not_leak(cuda, dt):
+    """Splits that lie past a query's length write only their (max, sum); the
+    output slots of such a split keep whatever the workspace held. Filled with
+    NaN bytes first, the workspace must still give the oracle's results."""
+    batch, hq, hkv, hd, max_seq = 6, 32, 8, 128, 8192
+    g = gen(77)
+    q = randn((batch, hq, hd), dt, g)
+    kc = randn((batch, hkv, max_seq, hd), dt, g)
+    vc = randn((batch, hkv, max_seq, hd), dt, g)
+    lens = torch.tensor([max_seq, 1, 100, 513, 2000, 7000], dtype=torch.int32)  # most splits of short queries empty
+    seq_ids = torch.arange(batch, dtype=torch.int32)
+    L = _lib.load()
+    need = ctypes.c_size_t()
+    _lib.check(L.bm_decode_attention_workspace_size(batch, hq, hkv, hd, max_seq, ctypes.byref(need)))
+    assert need.value > 0
+    ws = torch.full((need.value,), 0xFF, dtype=torch.uint8, device=cuda)  # every float a NaN
+    out = torch.empty((batch, hq, hd), dtype=dt, device=cuda)
+    qd, kd, vd, sd, ld = q.to(cuda), kc.to(cuda), vc.to(cuda), seq_ids.to(cuda), lens.to(cuda)
+    _lib.check(L.bm_decode_attention(out.data_ptr(), qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), sd.data_ptr(),
+                                     ld.data_ptr(), max_seq, batch, hq, hkv, hd, max_seq, batch, 0.0, ws.data_ptr(),
+                                     need.value, ops.bm_dtype(q), None, torch.cuda.current_stream(cuda).cuda_stream))
+    torch.cuda.synchronize(cuda)
+    assert torch.isfinite(out.float()).all()
+    want, bad = oracle_attention(q, kc, vc, seq_ids, lens)
+    assert bad == 0
+    assert orc.worst_error(to_np(out), want) <= TOL[dt]
+
+
 def test_reference_attention_cases(cuda):
     """The reference's three attention checks (tests/kernel_tests.cu:285-287):
     inputs U[-1,1], one query, heads = kv heads."""
