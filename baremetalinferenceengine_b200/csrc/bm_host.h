@@ -21,6 +21,10 @@ int check_launch(const char* what);
 // Streaming multiprocessors of the current device (cached per device).
 int sm_count();
 
+// c[M][N] = a[M][K] b[K][N] in fp32 on CUDA cores (gemm_f32.cu); host checks are
+// the caller's.
+int gemm_f32(float* c, const float* a, const float* b, int64_t m, int n, int k, cudaStream_t stream);
+
 // cudaFuncSetAttribute(kernel, MaxDynamicSharedMemorySize, bytes) on the current
 // device, once per (device, kernel): later calls cost a lookup, not a driver call.
 int allow_dynamic_smem(const void* kernel, int bytes, const char* what);

@@ -571,6 +571,15 @@ extern "C" int bm_gemm(void* c, const void* a, const void* b, int64_t m, int32_t
                        int32_t* d_status, void* stream) {
   using namespace bm;
   const char* what = "bm_gemm";
+  if (dtype == BM_F32) {  // fp32 operands: CUDA cores, any shape (gemm_f32.cu)
+    if (m < 0 || m > (int64_t{1} << 31) || n < 0 || k < 0) {
+      return fail(BM_ERR_INVALID_ARGUMENT, "%s: negative or too large size", what);
+    }
+    if (m == 0 || n == 0) return BM_OK;
+    if (!c || (k > 0 && (!a || !b))) return fail(BM_ERR_INVALID_ARGUMENT, "%s: NULL pointer", what);
+    return gemm_f32(static_cast<float*>(c), static_cast<const float*>(a), static_cast<const float*>(b), m, n, k,
+                    as_stream(stream));
+  }
   if (int st = gemm::check_shapes(what, m, n, k, dtype)) return st;
   return gemm::run<false>(what, c, a, b, b, m, n, k, d_status, stream);
 }

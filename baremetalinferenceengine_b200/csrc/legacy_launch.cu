@@ -89,3 +89,20 @@ void launch_attention(float* out, float* q, float* k_cache, float* v_cache, floa
                                        stream),
                   "launch_attention");
 }
+
+// Reference: include/kernels.cuh:20, src/kernels.cu:83-121. C[M][N] = A[M][K] B[K][N]
+// in fp32 (the engine calls it with M = 1 per token): bm_gemm's CUDA-core path.
+void launch_gemm(float* C, float* A, float* B, int M, int N, int K, cudaStream_t stream) {
+  if (M <= 0 || N <= 0) return;  // the reference's grid is empty
+  BM_LAUNCH_CHECK(bm_gemm(C, A, B, M, N, K < 0 ? 0 : K, BM_F32, nullptr, stream), "launch_gemm");
+}
+
+// Reference: include/kernels.cuh:23, src/kernels.cu:174-176.
+void launch_softmax(float* x, int size, cudaStream_t stream) { launch_softmax_batch(x, size, 1, size, stream); }
+
+// Reference: include/kernels.cuh:26, src/kernels.cu:178-180. num_vectors vectors of
+// `size` elements, `stride` apart, in place.
+void launch_softmax_batch(float* x, int size, int num_vectors, int stride, cudaStream_t stream) {
+  if (size <= 0 || num_vectors <= 0) return;
+  BM_LAUNCH_CHECK(bm_softmax(x, size, num_vectors, stride, BM_F32, stream), "launch_softmax_batch");
+}

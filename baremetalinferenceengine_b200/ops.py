@@ -217,7 +217,8 @@ def gemm_swiglu(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, out: 
 
 def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None,
          status: Optional[DeviceStatus] = None, stream=None) -> torch.Tensor:
-    """out = a @ b on the tensor cores (bf16): a [m, k], b [k, n] (launch_gemm's operand layout)."""
+    """out = a @ b: a [m, k], b [k, n] (launch_gemm's operand layout). bf16 runs on
+    the tensor cores; fp32 on CUDA cores (built for few rows)."""
     _dense(a, "a")
     _dense(b, "b")
     if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0]:
@@ -234,6 +235,20 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None,
         check(load().bm_gemm(_ptr(out), _ptr(a), _ptr(b), m, n, k, bm_dtype(a), status.ptr if status else None,
                              _stream(a.device, stream)))
     return out
+
+
+def softmax(x: torch.Tensor, size: Optional[int] = None, num_vectors: int = 1, stride: Optional[int] = None,
+            stream=None) -> torch.Tensor:
+    """In place: num_vectors vectors of `size` elements, `stride` apart, each
+    replaced by exp(x - max) / sum exp(x - max) (defaults: x as one vector)."""
+    _dense(x, "x")
+    size = x.numel() if size is None else size
+    stride = size if stride is None else stride
+    if num_vectors > 0 and size > 0 and (num_vectors - 1) * stride + size > x.numel():
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "vectors reach past x")
+    with torch.cuda.device(_dev(x)):
+        check(load().bm_softmax(_ptr(x), size, num_vectors, stride, bm_dtype(x), _stream(x.device, stream)))
+    return x
 
 
 def _positions(positions, rows):
@@ -325,6 +340,23 @@ def launch_rope(q: torch.Tensor, k: torch.Tensor, seq_pos: int, head_dim: int, n
     with torch.cuda.device(_dev(q)):
         check(load().bm_rope(_ptr(q), _ptr(k), None, seq_pos, None, 0, float(theta), 1, num_heads, num_kv_heads,
                              head_dim, _lib.BM_F32, None, _stream_arg(stream)))
+
+
+def launch_gemm(c: torch.Tensor, a: torch.Tensor, b: torch.Tensor, m: int, n: int, k: int, stream=0) -> None:
+    """include/kernels.cuh:20 — c[m][n] = a[m][k] b[k][n], fp32."""
+    with torch.cuda.device(_dev(a)):
+        check(load().bm_gemm(_ptr(c), _ptr(a), _ptr(b), m, n, k, _lib.BM_F32, None, _stream_arg(stream)))
+
+
+def launch_softmax_batch(x: torch.Tensor, size: int, num_vectors: int, stride: int, stream=0) -> None:
+    """include/kernels.cuh:26 — softmax in place over num_vectors vectors `stride` apart."""
+    with torch.cuda.device(_dev(x)):
+        check(load().bm_softmax(_ptr(x), size, num_vectors, stride, _lib.BM_F32, _stream_arg(stream)))
+
+
+def launch_softmax(x: torch.Tensor, size: int, stream=0) -> None:
+    """include/kernels.cuh:23 — softmax in place over one vector."""
+    launch_softmax_batch(x, size, 1, size, stream)
 
 
 def launch_swiglu(out: torch.Tensor, gate: torch.Tensor, up: torch.Tensor, size: int, stream=0) -> None:

@@ -240,11 +240,21 @@ int bm_decode_attention_static_scratch(void* out, const void* q, const void* k_c
  * FFN input projections and the SwiGLU of src/execution_engine.cu:122-124 in one
  * kernel, the products kept in fp32 until the SwiGLU. bm_gemm: c[M][N] = a[M][K] b[K][N].
  * A pipeline wait that passes its time limit (a fault, never a slow input) sets
- * BM_DEVERR_TIMEOUT in *d_status. */
+ * BM_DEVERR_TIMEOUT in *d_status.
+ * bm_gemm also takes BM_F32 (any M, N, K; no alignment needed): fp32 arithmetic on
+ * CUDA cores, built for few rows (the reference engine's one-token products,
+ * src/execution_engine.cu:81,110-125), K split over a thread-block cluster and
+ * reduced in a fixed order (deterministic); d_status is not used. */
 int bm_gemm_swiglu(void* out, const void* x, const void* w_gate, const void* w_up, int64_t rows, int32_t dim,
                    int32_t hidden, bm_dtype_t dtype, int32_t* d_status, void* stream);
 int bm_gemm(void* c, const void* a, const void* b, int64_t m, int32_t n, int32_t k, bm_dtype_t dtype,
             int32_t* d_status, void* stream);
+
+/* Softmax in place over num_vectors vectors of `size` elements, `stride`
+ * elements apart (the gaps untouched): x = exp(x - max) / sum exp(x - max), fp32
+ * arithmetic. Replaces launch_softmax(_batch) (include/kernels.cuh:23-26,
+ * src/kernels.cu:150-180). */
+int bm_softmax(void* x, int64_t size, int64_t num_vectors, int64_t stride, bm_dtype_t dtype, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Batch-aware static KV cache. Replaces the reference's KVCache

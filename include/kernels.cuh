@@ -1,10 +1,10 @@
-// kernels.cuh — drop-in launch API for BareMetalInferenceEngine's layer ops.
+// kernels.cuh — drop-in launch API for BareMetalInferenceEngine's kernels.
 //
 // These are C++ (name-mangled) functions with exactly the signatures of the
-// reference's include/kernels.cuh, so src/execution_engine.cu and its tests
-// compile unchanged against this header and link against libbm_layer_ops.so.
-// Each one is a single-token, fp32 call into the batched C ABI of
-// bm_layer_ops.h (rows = 1, dtype = BM_F32) on `stream`.
+// reference's include/kernels.cuh — all nine of them — so src/execution_engine.cu
+// and its tests compile unchanged against this header and link against
+// libbm_layer_ops.so alone. Each one is a single-token, fp32 call into the
+// batched C ABI of bm_layer_ops.h (rows = 1, dtype = BM_F32) on `stream`.
 //
 // Error behaviour follows the reference's CUDA_CHECK (include/cuda_utils.h:8-16):
 // an argument the reference would pass to a kernel that then writes out of
@@ -42,11 +42,12 @@ void launch_kv_store(float* cache, float* src, int seq_pos, int num_heads, int h
 // attention of bm_layer_ops.h, which keeps its per-split partials in `scores`.
 void launch_attention(float* out, float* q, float* k_cache, float* v_cache, float* scores, int num_heads, int head_dim, int max_seq_len, int seq_len, cudaStream_t stream = 0);
 
-// Not implemented in this library (outside the layer-op path). An engine built
-// against this header links these from the reference's src/kernels.cu compiled
-// with the six names above renamed away (the recipe is in INTEGRATION.md).
-// Reference include/kernels.cuh:20,23,26.
+// Reference include/kernels.cuh:20. C[M][N] = A[M][K] B[K][N], fp32 row-major,
+// any sizes: bm_gemm's fp32 path (CUDA cores, K split over a cluster).
 void launch_gemm(float* C, float* A, float* B, int M, int N, int K, cudaStream_t stream = 0);
+
+// Reference include/kernels.cuh:23,26. Softmax in place over one vector, or over
+// num_vectors vectors `stride` floats apart (the gaps untouched): bm_softmax.
 void launch_softmax(float* x, int size, cudaStream_t stream = 0);
 void launch_softmax_batch(float* x, int size, int num_vectors, int stride, cudaStream_t stream = 0);
 

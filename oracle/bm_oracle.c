@@ -26,6 +26,8 @@
  *                       id check of src/execution_engine.cu:63-65
  *   oracle_decode_attention  tests/kernel_tests.cu:229-258 (test_attention), batched, GQA
  *   oracle_gemm         tests/kernel_tests.cu:49-59 (reference_gemm)
+ *   oracle_softmax      tests/kernel_tests.cu:105-160 (the softmax checks): per vector,
+ *                       exp(x - max) / sum exp(x - max) in double
  *   oracle_gemm_swiglu  reference_gemm twice, then the SwiGLU of :122
  *                       (src/execution_engine.cu:122-124)
  *   oracle_layer_step(_mt)  the five ops above (or a chosen subset) over a row
@@ -531,4 +533,21 @@ void oracle_gemm(void* c, const void* a, const void* b, int64_t m, int64_t n, in
 void oracle_gemm_swiglu(void* out, const void* x, const void* w_gate, const void* w_up, int64_t rows, int64_t dim,
                         int64_t hidden, int dt, int threads) {
   gemm_mt(out, x, w_gate, w_up, rows, hidden, dim, dt, threads);
+}
+
+/* ------------------------------------------------------------------------- */
+/* Softmax in place (tests/kernel_tests.cu:105-160): for each of num_vectors   */
+/* vectors of `size` elements, `stride` apart, x = exp(x - max) / sum exp(x -   */
+/* max) with the sum in double, rounded once; the gaps are left untouched.      */
+void oracle_softmax(void* x, int64_t size, int64_t num_vectors, int64_t stride, int dt) {
+  for (int64_t v = 0; v < num_vectors; ++v) {
+    const int64_t off = v * stride;
+    double mx = -INFINITY, total = 0.0;
+    for (int64_t i = 0; i < size; ++i) {
+      const double e = ld(x, off + i, dt);
+      if (e > mx) mx = e;
+    }
+    for (int64_t i = 0; i < size; ++i) total += exp(ld(x, off + i, dt) - mx);
+    for (int64_t i = 0; i < size; ++i) st(x, off + i, exp(ld(x, off + i, dt) - mx) / total, dt);
+  }
 }

@@ -2,13 +2,8 @@
 // (include/kernels.cuh) served by the CPU oracle on host memory, for running
 // the reference's unmodified tests/kernel_tests.cu on a machine without a GPU
 // (with fake_cudart.cpp). The reference's own double-precision check loops then
-// grade the oracle: every check that has an oracle counterpart (rms_norm,
-// swiglu, rope, add, kv_store, attention, gemm) prints its worst error against
-// the oracle's output.
-//
-// launch_softmax(_batch) is outside the path; a plain loop stands in for it
-// here only so the harness runs to completion with the random-number sequence
-// it was written with.
+// grade the oracle: every check (rms_norm, softmax, swiglu, rope, add, kv_store,
+// attention, gemm) prints its worst error against the oracle's output.
 #include <cmath>
 #include <cstdint>
 #include <vector>
@@ -28,6 +23,7 @@ int32_t oracle_decode_attention(void* out, const void* q, const void* k_cache, c
                                 const int32_t* seq_ids, const int32_t* lens, int64_t batch, int hq, int hkv, int hd,
                                 int max_seq, int num_seqs, int dt);
 void oracle_gemm(void* c, const void* a, const void* b, int64_t m, int64_t n, int64_t k, int dt, int threads);
+void oracle_softmax(void* x, int64_t size, int64_t num_vectors, int64_t stride, int dt);
 }
 
 void launch_rms_norm(float* out, float* in, float* weight, int size, float eps, cudaStream_t) {
@@ -51,7 +47,7 @@ void launch_kv_store(float* cache, float* src, int seq_pos, int num_heads, int h
   oracle_kv_store(cache, src, nullptr, seq_pos, nullptr, 1, num_heads, head_dim, max_seq_len, 1, 0);
 }
 
-// ---- stand-ins outside the layer-op path ----
+// ---- GEMM, softmax and attention ----
 
 // The oracle's GEMM, so that the harness's test_gemm grades it against the
 // reference's own reference_gemm.
@@ -59,14 +55,9 @@ void launch_gemm(float* C, float* A, float* B, int M, int N, int K, cudaStream_t
   oracle_gemm(C, A, B, M, N, K, 0, 1);
 }
 
+// The oracle's softmax, graded by the harness's softmax checks (tests/kernel_tests.cu:105-160).
 void launch_softmax_batch(float* x, int size, int num_vectors, int stride, cudaStream_t) {
-  for (int v = 0; v < num_vectors; ++v) {
-    float* p = x + static_cast<size_t>(v) * stride;
-    double mx = -INFINITY, total = 0.0;
-    for (int i = 0; i < size; ++i) mx = p[i] > mx ? p[i] : mx;
-    for (int i = 0; i < size; ++i) total += std::exp(static_cast<double>(p[i]) - mx);
-    for (int i = 0; i < size; ++i) p[i] = static_cast<float>(std::exp(static_cast<double>(p[i]) - mx) / total);
-  }
+  oracle_softmax(x, size, num_vectors, stride, 0);
 }
 
 void launch_softmax(float* x, int size, cudaStream_t stream) { launch_softmax_batch(x, size, 1, size, stream); }

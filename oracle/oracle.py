@@ -76,6 +76,7 @@ def lib() -> ctypes.CDLL:
             "oracle_decode_attention": (i32, [vp, vp, vp, vp, vp, vp, i64, cint, cint, cint, cint, cint, cint]),
             "oracle_gemm": (None, [vp, vp, vp, i64, i64, i64, cint, cint]),
             "oracle_gemm_swiglu": (None, [vp, vp, vp, vp, i64, i64, i64, cint, cint]),
+            "oracle_softmax": (None, [vp, i64, i64, i64, cint]),
             "oracle_layer_step": (i32, [ctypes.POINTER(OracleStep), i64, i64]),
             "oracle_layer_step_mt": (i32, [ctypes.POINTER(OracleStep), i64, i64, cint]),
             "oracle_f32_to_bf16": (ctypes.c_uint16, [ctypes.c_float]),
@@ -242,6 +243,16 @@ def gemm_swiglu(x: np.ndarray, w_gate: np.ndarray, w_up: np.ndarray, threads: in
     out = np.empty((rows, hidden), x.dtype)
     lib().oracle_gemm_swiglu(_p(out), _p(x), _p(w_gate), _p(w_up), rows, dim, hidden, _dt(x), threads)
     return out
+
+
+def softmax(x: np.ndarray, size: int | None = None, num_vectors: int = 1, stride: int | None = None) -> np.ndarray:
+    """oracle_softmax (tests/kernel_tests.cu:105-160) on a copy of the flat array x:
+    num_vectors vectors of `size` elements, `stride` apart (gaps untouched)."""
+    out = np.array(x, copy=True, order="C").ravel()
+    size = out.size if size is None else size
+    stride = size if stride is None else stride
+    lib().oracle_softmax(_p(out), size, num_vectors, stride, _dt(out))
+    return out.reshape(np.shape(x))
 
 
 def layer_step(step: OracleStep, r0: int, r1: int, threads: int = 1) -> int:

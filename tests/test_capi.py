@@ -28,6 +28,9 @@ LEGACY = {
     "launch_add": "_Z10launch_addPfS_S_iP11CUstream_st",
     "launch_kv_store": "_Z15launch_kv_storePfS_iiiiP11CUstream_st",
     "launch_attention": "_Z16launch_attentionPfS_S_S_S_iiiiP11CUstream_st",
+    "launch_gemm": "_Z11launch_gemmPfS_S_iiiP11CUstream_st",
+    "launch_softmax": "_Z14launch_softmaxPfiP11CUstream_st",
+    "launch_softmax_batch": "_Z20launch_softmax_batchPfiiiP11CUstream_st",
 }
 
 
@@ -125,7 +128,6 @@ FAKE = 0x100000  # never dereferenced: every call below fails or returns before 
     lambda L: L.bm_kv_cache_layer(None, 0, ctypes.byref(ctypes.c_void_p()), ctypes.byref(ctypes.c_void_p())),
     lambda L: L.bm_kv_cache_seq_len(None, 0, ctypes.byref(ctypes.c_int32())),
     lambda L: L.bm_kv_cache_reset(None, 0),
-    lambda L: L.bm_gemm(FAKE, FAKE, FAKE, 4, 64, 64, 0, None, None),                  # fp32: tensor cores take bf16
     lambda L: L.bm_gemm(FAKE, FAKE, FAKE, 3, 5, 7, 1, None, None),                    # N, K not multiples of 8
     lambda L: L.bm_gemm(FAKE, FAKE, FAKE, 4, 64, 60, 1, None, None),                  # K not a multiple of 8
     lambda L: L.bm_gemm(FAKE, FAKE, FAKE, -1, 64, 64, 1, None, None),                 # negative rows
@@ -134,6 +136,12 @@ FAKE = 0x100000  # never dereferenced: every call below fails or returns before 
     lambda L: L.bm_gemm_swiglu(FAKE, FAKE, FAKE, FAKE, 4, 64, 64, 0, None, None),    # fp32
     lambda L: L.bm_gemm_swiglu(FAKE, FAKE, FAKE, FAKE, 4, 64, 60, 1, None, None),    # hidden % 8
     lambda L: L.bm_gemm_swiglu(FAKE, FAKE, FAKE, None, 4, 64, 64, 1, None, None),    # NULL w_up
+    lambda L: L.bm_gemm(FAKE, None, FAKE, 4, 5, 7, 0, None, None),                    # fp32: NULL operand
+    lambda L: L.bm_gemm(FAKE, FAKE, FAKE, -1, 5, 7, 0, None, None),                   # fp32: negative rows
+    lambda L: L.bm_softmax(FAKE, 8, 2, 4, 0, None),                                   # stride < size
+    lambda L: L.bm_softmax(FAKE, -1, 1, 8, 0, None),                                  # negative size
+    lambda L: L.bm_softmax(None, 8, 1, 8, 0, None),                                   # NULL x
+    lambda L: L.bm_softmax(FAKE, 8, 1, 8, 9, None),                                   # bad dtype
 ])
 def test_host_checks_reject_before_any_launch(lib, call):
     assert call(lib) == _lib.BM_ERR_INVALID_ARGUMENT
@@ -154,6 +162,9 @@ def test_host_checks_reject_before_any_launch(lib, call):
     lambda L: L.bm_kv_cache_destroy(None),
     lambda L: L.bm_gemm(FAKE, FAKE, FAKE, 0, 64, 64, 1, None, None),
     lambda L: L.bm_gemm_swiglu(FAKE, FAKE, FAKE, FAKE, 0, 64, 64, 1, None, None),
+    lambda L: L.bm_gemm(FAKE, FAKE, FAKE, 0, 5, 7, 0, None, None),
+    lambda L: L.bm_softmax(FAKE, 0, 4, 8, 0, None),
+    lambda L: L.bm_softmax(FAKE, 8, 0, 8, 0, None),
 ])
 def test_empty_calls_are_no_ops(lib, call):
     assert call(lib) == _lib.BM_OK

@@ -50,7 +50,7 @@ def test_reference_benchmark_generates_the_same_tokens_on_every_build(cuda, tmp_
     write_export(str(tmp_path), seed=31)
     results = {}
     for name, exe in [("reference", os.path.join(orc.REF_DIR, "benchmark_ref")),
-                      ("reference engine + B200 layer ops", os.path.join(orc.REF_DIR, "benchmark_dropin")),
+                      ("reference engine + B200 kernels", os.path.join(orc.REF_DIR, "benchmark_dropin")),
                       ("fused engine", os.path.join(ENGINE_BUILD, "benchmark_fused"))]:
         out = tmp_path / (name.split()[0] + str(len(results)) + ".json")
         proc = subprocess.run([need(exe), str(tmp_path), str(out)], capture_output=True, text=True, timeout=900)

@@ -136,7 +136,63 @@ def test_full_size_prefill_ffn_sampled_rows(cuda):
     assert orc.worst_error(to_np(out[sample.to(cuda)]), want) <= BF16_TOL
 
 
-def test_fp32_is_refused(cuda):
-    a = torch.zeros(16, 16, device=cuda)
-    with pytest.raises(_lib.BMError):
-        ops.gemm(a, a)
+@pytest.mark.parametrize("m,n,k", [
+    (16, 16, 16), (128, 128, 128), (3, 5, 7), (17, 33, 65), (1, 4096, 4096),  # tests/kernel_tests.cu:263-267
+    (1, 32000, 288), (1, 288, 288), (1, 768, 288), (1, 288, 768),            # the engine's one-token products
+    (7, 300, 200), (9, 130, 4100), (40, 1000, 96),                           # ragged rows, long K, many rows
+])
+def test_fp32_gemm_matches_the_oracle(cuda, m, n, k):
+    """fp32 (the reference's launch_gemm path): CUDA cores, any shape, within 1e-5."""
+    g = gen(m + 3 * n + 7 * k)
+    a = torch.rand(m, k, generator=g) * 2 - 1
+    b = torch.rand(k, n, generator=g) * 2 - 1
+    c = torch.full((m, n), float("nan"), device=cuda)
+    ops.launch_gemm(c, a.to(cuda), b.to(cuda), m, n, k)
+    torch.cuda.synchronize(cuda)
+    want = orc.gemm(a.numpy(), b.numpy(), threads=8)
+    assert orc.worst_error(c.cpu().numpy(), want) <= 1e-5
+    again = ops.gemm(a.to(cuda), b.to(cuda))  # deterministic: the cluster adds its partials in a fixed order
+    assert torch.equal(again.cpu(), c.cpu())
+
+
+def test_fp32_gemm_misaligned_operands(cuda):
+    """Rows of B that are not 16-byte multiples, and a B that starts off a 16-byte boundary."""
+    g = gen(5)
+    m, n, k = 4, 129, 77
+    a = (torch.rand(m, k, generator=g) * 2 - 1).to(cuda)
+    store = (torch.rand(k * n + 1, generator=g) * 2 - 1).to(cuda)
+    b = store[1:].view(k, n)
+    c = torch.empty(m, n, device=cuda)
+    ops.launch_gemm(c, a, b, m, n, k)
+    torch.cuda.synchronize(cuda)
+    want = orc.gemm(a.cpu().numpy(), b.cpu().numpy().copy())
+    assert orc.worst_error(c.cpu().numpy(), want) <= 1e-5
+
+
+@pytest.mark.parametrize("size,vectors,stride,lo,hi", [
+    (1, 1, 1, -4, 4), (100, 1, 100, -4, 4), (4096, 1, 4096, -4, 4),   # tests/kernel_tests.cu:268-275
+    (1000, 1, 1000, 995, 1005),                                         # values near 1000 (:140-147)
+    (37, 5, 50, -4, 4),                                                 # batch with gaps (:149-160)
+    (32000, 3, 32000, -20, 20), (128256, 1, 128256, -10, 10),          # vocab-sized rows
+])
+def test_softmax_matches_the_oracle(cuda, size, vectors, stride, lo, hi):
+    g = gen(size + vectors)
+    x = torch.rand((vectors - 1) * stride + size, generator=g) * (hi - lo) + lo
+    xd = x.to(cuda)
+    ops.launch_softmax_batch(xd, size, vectors, stride)
+    torch.cuda.synchronize(cuda)
+    want = orc.softmax(x.numpy(), size, vectors, stride)
+    assert orc.worst_error(xd.cpu().numpy(), want) <= 1e-5
+    for v in range(vectors - 1):  # the gaps between vectors are untouched
+        gap = slice(v * stride + size, (v + 1) * stride)
+        assert torch.equal(xd.cpu()[gap], x[gap])
+
+
+def test_softmax_bf16(cuda):
+    g = gen(3)
+    x = (torch.randn(4, 1000, generator=g) * 3).to(torch.bfloat16)
+    xd = x.to(cuda)
+    ops.softmax(xd.view(-1), 1000, 4, 1000)
+    torch.cuda.synchronize(cuda)
+    want = orc.softmax(to_np(x).ravel(), 1000, 4, 1000)
+    assert orc.worst_error(to_np(xd).ravel(), want) <= 1e-2

@@ -49,6 +49,10 @@ def test_reference_harness_grades_the_oracle():
         err = float(re.search(r"worst relative error (\S+)", line).group(1))
         # exact everywhere except the known-answer test, whose want rounds silu(-100)*2 (~7e-42) to 0
         assert err == 0.0 or ("stays finite" in line and err < 1e-40), line
+    softmax = [l for l in lines if l[6:].startswith("softmax")]
+    assert len(softmax) == 5, softmax  # kernel_tests.cu: sizes 1, 100, 4096, near 1000, batch with gaps
+    for line in softmax:
+        assert line.startswith("PASS") and float(re.search(r"worst relative error (\S+)", line).group(1)) == 0.0, line
     gemm = [l for l in lines if l[6:].startswith("gemm")]
     assert len(gemm) == 5, gemm  # kernel_tests.cu:263-267, served by oracle_gemm
     for line in gemm:
