@@ -35,12 +35,17 @@ ExecutionEngine::ExecutionEngine(std::shared_ptr<MemoryAllocator> allocator, std
   logits_ = std::make_shared<DeviceBuffer<float>>(config_.vocab_size);
   // (cos, sin) per position, computed once on the device in fp64 and kept in L2-sized fp32
   rope_table_ = std::make_shared<DeviceBuffer<float>>(static_cast<size_t>(max_seq) * config_.head_dim());
-  check(bm_rope_table_fill(rope_table_->get(), max_seq, config_.head_dim(), config_.rope_theta, nullptr),
+  CUDA_CHECK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+  check(bm_rope_table_fill(rope_table_->get(), max_seq, config_.head_dim(), config_.rope_theta, stream_),
         "bm_rope_table_fill");
   reserve(1);
 }
 
-ExecutionEngine::~ExecutionEngine() {}
+ExecutionEngine::~ExecutionEngine() {
+  if (decode_graph_) cudaGraphExecDestroy(decode_graph_);
+  if (staging_) cudaFreeHost(staging_);
+  if (stream_) cudaStreamDestroy(stream_);
+}
 
 float* ExecutionEngine::weight(const std::string& name) const {
   float* tensor = static_cast<float*>(allocator_->get_device_tensor(name));
@@ -69,7 +74,10 @@ void ExecutionEngine::reserve(int tokens) {
   up_ = buffer(n * hidden);
   activated_ = buffer(n * hidden);
   ids_ = std::make_shared<DeviceBuffer<int>>(n);
+  positions_ = std::make_shared<DeviceBuffer<int>>(n);
   lens_ = std::make_shared<DeviceBuffer<int>>(n);
+  if (staging_) CUDA_CHECK(cudaFreeHost(staging_));
+  CUDA_CHECK(cudaMallocHost(&staging_, 3 * n * sizeof(int)));
   size_t ws = 0;
   check(bm_decode_attention_workspace_size(tokens, config_.num_heads, config_.num_heads, config_.head_dim(),
                                            kv_cache_->get_max_seq_len(), &ws),
@@ -97,20 +105,67 @@ std::vector<float> ExecutionEngine::forward(const std::vector<int>& input_tokens
 
   const int T = static_cast<int>(input_tokens.size());
   reserve(T);
+  const int pos0 = kv_cache_->get_current_seq_pos();
+  // ids, positions and attended lengths (token t: pos0 + t + 1) via pinned staging
+  for (int t = 0; t < T; ++t) {
+    staging_[t] = input_tokens[t];
+    staging_[capacity_ + t] = pos0 + t;
+    staging_[2 * capacity_ + t] = pos0 + t + 1;
+  }
+  CUDA_CHECK(cudaMemcpyAsync(ids_->get(), staging_, sizeof(int) * T, cudaMemcpyHostToDevice, stream_));
+  CUDA_CHECK(cudaMemcpyAsync(positions_->get(), staging_ + capacity_, sizeof(int) * T, cudaMemcpyHostToDevice,
+                             stream_));
+  CUDA_CHECK(cudaMemcpyAsync(lens_->get(), staging_ + 2 * capacity_, sizeof(int) * T, cudaMemcpyHostToDevice,
+                             stream_));
+
+  if (T > 1) {
+    run(T, pos0 + T);
+  } else if (decode_graph_ && graph_capacity_ == capacity_) {
+    CUDA_CHECK(cudaGraphLaunch(decode_graph_, stream_));
+  } else if (eager_decode_steps_ < 1 || graph_capacity_ >= 0) {
+    // the first decode step runs eagerly (it sets up every kernel outside a
+    // capture); so does every step after the buffers moved under a graph
+    ++eager_decode_steps_;
+    if (decode_graph_ && graph_capacity_ != capacity_) {
+      CUDA_CHECK(cudaGraphExecDestroy(decode_graph_));
+      decode_graph_ = nullptr;
+      graph_capacity_ = -1;
+    }
+    run(1, max_seq);
+  } else {
+    cudaGraph_t graph = nullptr;
+    CUDA_CHECK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    try {
+      run(1, max_seq);
+    } catch (...) {
+      cudaStreamEndCapture(stream_, &graph);
+      if (graph) cudaGraphDestroy(graph);
+      throw;
+    }
+    CUDA_CHECK(cudaStreamEndCapture(stream_, &graph));
+    CUDA_CHECK(cudaGraphInstantiate(&decode_graph_, graph, 0));
+    CUDA_CHECK(cudaGraphDestroy(graph));
+    graph_capacity_ = capacity_;
+    CUDA_CHECK(cudaGraphLaunch(decode_graph_, stream_));
+  }
+  kv_cache_->increment_seq_pos(T);
+
+  std::vector<float> logits(config_.vocab_size);
+  CUDA_CHECK(cudaMemcpyAsync(logits.data(), logits_->get(), logits.size() * sizeof(float), cudaMemcpyDeviceToHost,
+                             stream_));
+  CUDA_CHECK(cudaStreamSynchronize(stream_));
+  return logits;
+}
+
+void ExecutionEngine::run(int T, int max_len) {
   const int dim = config_.dim;
   const int hidden_dim = config_.hidden_dim;
   const int heads = config_.num_heads;
   const int head_dim = config_.head_dim();
-  const int pos0 = kv_cache_->get_current_seq_pos();
+  const int max_seq = kv_cache_->get_max_seq_len();
   const float eps = config_.norm_eps;
-
-  CUDA_CHECK(cudaMemcpy(ids_->get(), input_tokens.data(), sizeof(int) * T, cudaMemcpyHostToDevice));
-  // token t attends to the positions up to its own: pos0 + t + 1 of them
-  std::vector<int> lens(T);
-  for (int t = 0; t < T; ++t) lens[t] = pos0 + t + 1;
-  CUDA_CHECK(cudaMemcpy(lens_->get(), lens.data(), sizeof(int) * T, cudaMemcpyHostToDevice));
   check(bm_embed_gather(hidden_, token_embeddings_, ids_->get(), T, dim, config_.vocab_size, dim, BM_F32, nullptr,
-                        nullptr),
+                        stream_),
         "bm_embed_gather");
 
   for (int l = 0; l < config_.num_layers; ++l) {
@@ -120,40 +175,37 @@ std::vector<float> ExecutionEngine::forward(const std::vector<int>& input_tokens
 
     // The previous layer's residual add (its down projection) is fused into this norm.
     if (l == 0) {
-      check(bm_rmsnorm(normed_, hidden_, w.attention_norm, T, dim, eps, dim, dim, BM_F32, nullptr), "bm_rmsnorm");
+      check(bm_rmsnorm(normed_, hidden_, w.attention_norm, T, dim, eps, dim, dim, BM_F32, stream_), "bm_rmsnorm");
     } else {
-      check(bm_add_rmsnorm(hidden_, projected_, w.attention_norm, normed_, T, dim, eps, BM_F32, nullptr),
+      check(bm_add_rmsnorm(hidden_, projected_, w.attention_norm, normed_, T, dim, eps, BM_F32, stream_),
             "bm_add_rmsnorm");
     }
-    launch_gemm(q_, normed_, w.q_proj, T, dim, dim);
-    launch_gemm(k_, normed_, w.k_proj, T, dim, dim);
-    launch_gemm(v_, normed_, w.v_proj, T, dim, dim);
-    // Positions pos0..pos0+T-1 of the one sequence the reference's cache holds.
-    check(bm_rope_kv_store(q_, k_, v_, nullptr, pos0, nullptr, k_cache, v_cache, rope_table_->get(), max_seq,
-                           config_.rope_theta, T, heads, heads, head_dim, max_seq, 1, BM_F32, nullptr, nullptr),
+    launch_gemm(q_, normed_, w.q_proj, T, dim, dim, stream_);
+    launch_gemm(k_, normed_, w.k_proj, T, dim, dim, stream_);
+    launch_gemm(v_, normed_, w.v_proj, T, dim, dim, stream_);
+    // Token t at cache position positions_[t] of the one sequence the reference's cache holds.
+    check(bm_rope_kv_store(q_, k_, v_, positions_->get(), 0, nullptr, k_cache, v_cache, rope_table_->get(),
+                           max_seq, config_.rope_theta, T, heads, heads, head_dim, max_seq, 1, BM_F32, nullptr,
+                           stream_),
           "bm_rope_kv_store");
-    // All T tokens' attention in one launch: query t over cache positions [0, pos0 + t].
-    check(bm_decode_attention(attention_out_, q_, k_cache, v_cache, nullptr, lens_->get(), pos0 + T, T, heads,
+    // All T tokens' attention in one launch: query t over cache positions [0, lens_[t]).
+    check(bm_decode_attention(attention_out_, q_, k_cache, v_cache, nullptr, lens_->get(), max_len, T, heads,
                               heads, head_dim, max_seq, 1, 0.f, attention_workspace_->get(),
-                              attention_workspace_->size(), BM_F32, nullptr, nullptr),
+                              attention_workspace_->size(), BM_F32, nullptr, stream_),
           "bm_decode_attention");
-    launch_gemm(projected_, attention_out_, w.o_proj, T, dim, dim);
-    check(bm_add_rmsnorm(hidden_, projected_, w.ffn_norm, normed_, T, dim, eps, BM_F32, nullptr), "bm_add_rmsnorm");
-    launch_gemm(gate_, normed_, w.gate_proj, T, hidden_dim, dim);
-    launch_gemm(up_, normed_, w.up_proj, T, hidden_dim, dim);
-    check(bm_swiglu(activated_, gate_, up_, static_cast<int64_t>(T) * hidden_dim, BM_F32, nullptr), "bm_swiglu");
-    launch_gemm(projected_, activated_, w.down_proj, T, dim, hidden_dim);
+    launch_gemm(projected_, attention_out_, w.o_proj, T, dim, dim, stream_);
+    check(bm_add_rmsnorm(hidden_, projected_, w.ffn_norm, normed_, T, dim, eps, BM_F32, stream_), "bm_add_rmsnorm");
+    launch_gemm(gate_, normed_, w.gate_proj, T, hidden_dim, dim, stream_);
+    launch_gemm(up_, normed_, w.up_proj, T, hidden_dim, dim, stream_);
+    check(bm_swiglu(activated_, gate_, up_, static_cast<int64_t>(T) * hidden_dim, BM_F32, stream_), "bm_swiglu");
+    launch_gemm(projected_, activated_, w.down_proj, T, dim, hidden_dim, stream_);
   }
 
   // Only the last token's logits are returned: its final residual add and norm.
   const size_t last = static_cast<size_t>(T - 1) * dim;
   check(bm_add_rmsnorm(hidden_ + last, projected_ + last, final_norm_, normed_ + last, 1, dim, eps, BM_F32,
-                       nullptr),
+                       stream_),
         "bm_add_rmsnorm");
-  launch_gemm(logits_->get(), normed_ + last, lm_head_, 1, config_.vocab_size, dim);
-  kv_cache_->increment_seq_pos(T);
-
-  std::vector<float> logits(config_.vocab_size);
-  CUDA_CHECK(cudaMemcpy(logits.data(), logits_->get(), logits.size() * sizeof(float), cudaMemcpyDeviceToHost));
-  return logits;
+  launch_gemm(logits_->get(), normed_ + last, lm_head_, 1, config_.vocab_size, dim, stream_);
 }
+

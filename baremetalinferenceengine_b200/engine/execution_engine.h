@@ -13,10 +13,16 @@
 //     embedding gather, the residual add fused into the RMSNorm that follows it
 //     (:118+:121, :126+:109, :126+:80), RoPE fused with both KV-cache writes
 //     (:113-115), and the split decode attention (:116).
-// The GEMMs stay the reference's (launch_gemm from its src/kernels.cu): they are
-// outside the layer-op path.
+// The projections use this library's fp32 launch_gemm. Every launch goes to the
+// engine's own stream, and a one-token forward (a decode step) replays a CUDA
+// graph of the whole layer loop, captured on the second such call: positions and
+// attended lengths come from small device arrays refreshed before each replay,
+// and attention is planned for the cache's full length so the launches never
+// change.
 #ifndef EXECUTION_ENGINE_H
 #define EXECUTION_ENGINE_H
+
+#include <cuda_runtime.h>
 
 #include <memory>
 #include <string>
@@ -83,6 +89,16 @@ class ExecutionEngine {
   float* up_ = nullptr;
   float* activated_ = nullptr;
   std::shared_ptr<DeviceBuffer<int>> ids_;
+  // Every layer and the logits of the last token for T tokens on stream_;
+  // attention planned for at most max_len attended positions.
+  void run(int T, int max_len);
+
+  cudaStream_t stream_ = nullptr;
+  cudaGraphExec_t decode_graph_ = nullptr;  // a one-token forward, replayed
+  int graph_capacity_ = -1;                 // capacity_ when the graph was captured
+  int eager_decode_steps_ = 0;              // one-token forwards run before the capture
+  int* staging_ = nullptr;                  // pinned host: ids, positions, lens of a call
+  std::shared_ptr<DeviceBuffer<int>> positions_;           // cache position per token
   std::shared_ptr<DeviceBuffer<int>> lens_;                // attended positions per token
   std::shared_ptr<DeviceBuffer<char>> attention_workspace_;  // split partials of decode attention
 
