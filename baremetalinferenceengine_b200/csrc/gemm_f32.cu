@@ -83,13 +83,11 @@ __global__ void __launch_bounds__(kThreads) gemm_f32_kernel(const Args p) {
       for (int e = 0; e < 4; ++e) acc[r][e] = fmaf(av, bv[e], acc[r][e]);
     }
   };
-  // warp w takes k = kb + w, kb + w + 8, ...; four steps' loads in flight together
+  // warp w takes k = kb + w, kb + w + 8, ...; eight steps' loads in flight together
   int k = kb + warp;
-  for (; k + 3 * kWarps < ke; k += 4 * kWarps) {
-    step(k);
-    step(k + kWarps);
-    step(k + 2 * kWarps);
-    step(k + 3 * kWarps);
+  for (; k + 7 * kWarps < ke; k += 8 * kWarps) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) step(k + u * kWarps);
   }
   for (; k < ke; k += kWarps) step(k);
 
@@ -152,10 +150,10 @@ int gemm_f32(float* c, const float* a, const float* b, int64_t m, int n, int k, 
   const int64_t row_tiles = (m + mt - 1) / mt;
   if (row_tiles > 65535) return fail(BM_ERR_INVALID_ARGUMENT, "bm_gemm (fp32): more than %d rows", 65535 * 8);
   const int col_blocks = (n + kCols - 1) / kCols;
-  // split K over a cluster until the grid covers the GPU twice, keeping >= 64 k per warp group
+  // split K over a cluster until the grid covers the GPU twice, keeping >= 64 k per CTA
   const int64_t base = static_cast<int64_t>(col_blocks) * row_tiles;
   int ks = static_cast<int>(std::min<int64_t>(kMaxCluster, (2 * sm_count() + base - 1) / base));
-  ks = std::max(1, std::min(ks, (k + 511) / 512));
+  ks = std::max(1, std::min(ks, (k + 63) / 64));
   Args p{c, a, b, static_cast<int>(m), n, k, (k + ks - 1) / ks};
   const bool vec = n % 4 == 0 && aligned16(b);
   switch (mt) {
