@@ -27,6 +27,9 @@
 namespace bm {
 namespace attn {
 
+#ifndef BM_ATTN_BALANCED
+#define BM_ATTN_BALANCED 1  // bf16 head_dim 128: the balanced persistent kernel when it applies
+#endif
 #ifndef BM_ATTN_STAGED_MIN_TILES
 #define BM_ATTN_STAGED_MIN_TILES 4
 #endif
@@ -102,6 +105,17 @@ int decode_attention(void* out, const void* q, const void* k_cache, const void* 
   a.qscale = scale * 1.4426950408889634f;  // scores in base 2: exp(x) = exp2(x * log2(e))
   a.status = d_status;
   const bool tc = tc_eligible(a, dtype);
+  cudaStream_t s = as_stream(stream);
+  if (BM_ATTN_BALANCED && balanced_eligible(a, dtype) && workspace != nullptr &&
+      reinterpret_cast<uintptr_t>(workspace) % 16 == 0) {
+    // one CTA per SM, no more than there are tiles
+    const int64_t tiles = batch * hkv * ((max_len + kThreads - 1) / kThreads);
+    const int ctas = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(sm_count(), tiles)));
+    if (workspace_size >= balanced_workspace_bytes(a.group, ctas)) {
+      a.ws = static_cast<float*>(workspace);
+      return launch_tc_balanced(a, ctas, s);
+    }
+  }
   plan_splits(batch * hkv, max_len, sm_count(), &a.splits, &a.split_len,
               tc || f32_tma_eligible(a, dtype) ? kStagedMinTiles : 1);
   const size_t need = workspace_bytes(batch, hkv, a.group, hd, a.splits);
@@ -115,7 +129,6 @@ int decode_attention(void* out, const void* q, const void* k_cache, const void* 
     a.splits = (tiles + tiles_per_split - 1) / tiles_per_split;
   }
   a.ws = a.splits > 1 ? static_cast<float*>(workspace) : nullptr;
-  cudaStream_t s = as_stream(stream);
   if (tc) return launch_tc(a, s);
   if (f32_tma_eligible(a, dtype)) return launch_f32_tma(a, s);
   return dtype == BM_F32 ? launch_f32(a, s) : launch_bf16(a, s);
@@ -125,7 +138,14 @@ size_t decode_attention_workspace(int64_t batch, int32_t hq, int32_t hkv, int32_
   if (batch <= 0 || hkv <= 0 || hq % hkv != 0 || max_len <= 0) return 0;
   int splits = 1, split_len = 0;
   plan_splits(batch * hkv, max_len, sm_count(), &splits, &split_len);
-  return workspace_bytes(batch, hkv, hq / hkv, hd, splits);
+  size_t bytes = workspace_bytes(batch, hkv, hq / hkv, hd, splits);
+  // a bf16 cache may take the balanced path, which needs its records and partials
+  // whenever a pair has more than one tile
+  if (BM_ATTN_BALANCED && hd == 128 && hq / hkv <= kMaxGroup && batch <= kBalancedMaxBatch &&
+      batch * hkv >= kBalancedMinPairs && max_len > kThreads) {
+    bytes = std::max(bytes, balanced_workspace_bytes(hq / hkv, sm_count()));
+  }
+  return bytes;
 }
 
 }  // namespace bm

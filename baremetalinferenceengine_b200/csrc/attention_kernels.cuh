@@ -441,6 +441,17 @@ int launch_bf16(const AttnArgs& a, cudaStream_t stream);
 bool tc_eligible(const AttnArgs& a, bm_dtype_t dtype);
 int launch_tc(const AttnArgs& a, cudaStream_t stream);
 
+// Its balanced persistent form (attention_tc_balanced.cu): one CTA per SM over an
+// equal share of all (query, kv head) tiles, for batches of at most
+// kBalancedMaxBatch queries and at least kBalancedMinPairs (query, kv head)
+// pairs (fewer pairs are split evenly by the per-pair grid already, which starts
+// faster); workspace: balanced_workspace_bytes(group, ctas).
+constexpr int kBalancedMaxBatch = 2048;
+constexpr int kBalancedMinPairs = 32;
+bool balanced_eligible(const AttnArgs& a, bm_dtype_t dtype);
+size_t balanced_workspace_bytes(int group, int ctas);
+int launch_tc_balanced(AttnArgs a, int ctas, cudaStream_t stream);
+
 // The TMA-fed CUDA-core kernel (attention_f32_tma.cu): fp32 caches with head_dim 128.
 bool f32_tma_eligible(const AttnArgs& a, bm_dtype_t dtype);
 int launch_f32_tma(const AttnArgs& a, cudaStream_t stream);
