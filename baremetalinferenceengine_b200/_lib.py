@@ -27,6 +27,7 @@ BM_BF16 = 1
 BM_DEVERR_BAD_ID = 0x1
 BM_DEVERR_BAD_POSITION = 0x2
 BM_DEVERR_BAD_SEQUENCE = 0x4
+BM_DEVERR_TIMEOUT = 0x8
 
 # name -> (restype, argtypes). Every symbol include/bm_layer_ops.h declares.
 SIGNATURES = {
@@ -72,6 +73,7 @@ SIGNATURES = {
     "bm_kv_cache_reset": (c_int, [c_void_p, c_int32]),
     "bm_kv_cache_append": (c_int, [c_void_p, c_void_p, c_int64, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p),
                                    c_void_p]),
+    "bm_selftest_bounded_wait": (c_int, [c_int64, c_void_p, c_void_p, c_void_p]),
 }
 
 _lock = threading.Lock()

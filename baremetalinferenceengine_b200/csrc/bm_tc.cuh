@@ -28,18 +28,6 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-// Non-blocking: true when the phase with this parity has completed.
-__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
@@ -52,9 +40,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// Polls of one wait past which it gives up even if the clock were to stall.
+constexpr uint32_t kMaxWaitPolls = 1u << 26;
+
 // Waits until the phase of `bar` with parity `parity` has completed. Returns
 // false when another role has aborted, or (setting the abort flag and the status
-// bit) when `limit_ns` passes; `honour_abort` = false waits out the limit anyway.
+// bit) when `limit_ns` passes or after kMaxWaitPolls polls; `honour_abort` =
+// false waits out the limit anyway.
 static __device__ __noinline__ bool wait_phase(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int32_t* status,
                                         uint64_t limit_ns, bool honour_abort) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -63,7 +55,7 @@ static __device__ __noinline__ bool wait_phase(uint64_t* bar, uint32_t parity, v
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 31) == 0) {
       if (honour_abort && *abort_flag) return false;
-      if (global_ns() - t0 > limit_ns) {
+      if (global_ns() - t0 > limit_ns || i >= kMaxWaitPolls) {
         *abort_flag = 1;
         raise_status(status, BM_DEVERR_TIMEOUT);
         return false;

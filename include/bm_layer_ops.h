@@ -288,6 +288,15 @@ int bm_kv_cache_reset(bm_kv_cache_t* cache, int32_t seq);
 int bm_kv_cache_append(bm_kv_cache_t* cache, const int32_t* seq_ids, int64_t rows,
                        const int32_t** positions_dev, const int32_t** seq_ids_dev, void* stream);
 
+/* Self-test of the bounded waits behind BM_DEVERR_TIMEOUT (the tensor-core
+ * kernels' mbarrier waits): one CTA waits on a barrier that nothing completes,
+ * with a limit of limit_ns in [1 ms, 2 s]. The wait gives up, ORs
+ * BM_DEVERR_TIMEOUT into *d_status and the kernel finishes; the context stays
+ * usable. d_result (device, 4 x int64): [0] 1 if the wait reported success
+ * (expected 0), [1] its duration in ns (about limit_ns), [2] and [3] the same for
+ * a second wait that honours the first one's abort (gives up at once). */
+int bm_selftest_bounded_wait(int64_t limit_ns, int32_t* d_status, int64_t* d_result, void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

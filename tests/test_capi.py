@@ -142,6 +142,9 @@ FAKE = 0x100000  # never dereferenced: every call below fails or returns before 
     lambda L: L.bm_softmax(FAKE, -1, 1, 8, 0, None),                                  # negative size
     lambda L: L.bm_softmax(None, 8, 1, 8, 0, None),                                   # NULL x
     lambda L: L.bm_softmax(FAKE, 8, 1, 8, 9, None),                                   # bad dtype
+    lambda L: L.bm_selftest_bounded_wait(1000, FAKE, FAKE, None),                     # limit below 1 ms
+    lambda L: L.bm_selftest_bounded_wait(10**10, FAKE, FAKE, None),                   # limit above 2 s
+    lambda L: L.bm_selftest_bounded_wait(50 * 10**6, None, FAKE, None),               # NULL status
 ])
 def test_host_checks_reject_before_any_launch(lib, call):
     assert call(lib) == _lib.BM_ERR_INVALID_ARGUMENT
