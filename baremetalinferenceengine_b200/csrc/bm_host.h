@@ -21,9 +21,16 @@ int check_launch(const char* what);
 // Streaming multiprocessors of the current device (cached per device).
 int sm_count();
 
-// c[M][N] = a[M][K] b[K][N] in fp32 on CUDA cores (gemm_f32.cu); host checks are
-// the caller's.
+// fp32 GEMMs on CUDA cores (gemm_f32.cu); host checks are the caller's.
+// c[M][N] = a[M][K] b[K][N].
 int gemm_f32(float* c, const float* a, const float* b, int64_t m, int n, int k, cudaStream_t stream);
+// c[o][M][n[o]] = a[M][K] b[o][K][n[o]] for o < count <= kMaxSharedA, one launch.
+constexpr int kMaxSharedA = 3;
+int gemm_f32_shared_a(float* const* c, const float* a, const float* const* b, const int32_t* n, int count,
+                      int64_t m, int k, cudaStream_t stream);
+// out[rows][hidden] = silu(x w_gate) * (x w_up), x [rows][dim], w_* [dim][hidden].
+int gemm_f32_swiglu(float* out, const float* x, const float* w_gate, const float* w_up, int64_t rows, int hidden,
+                    int dim, cudaStream_t stream);
 
 // cudaFuncSetAttribute(kernel, MaxDynamicSharedMemorySize, bytes) on the current
 // device, once per (device, kernel): later calls cost a lookup, not a driver call.

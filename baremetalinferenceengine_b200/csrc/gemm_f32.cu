@@ -10,7 +10,17 @@
 // its 8 warps take interleaved k, and a cluster of KS CTAs splits K further. The
 // warps' partial sums meet in shared memory; the cluster's CTAs then add theirs
 // in a fixed order through distributed shared memory, so results are
-// deterministic and no global scratch is needed.
+// deterministic and no global scratch is needed. Each warp runs its k steps in
+// unrolled rounds of eight. When a CTA's K range is short (a few rounds), every
+// load of a round is issued before its first multiply-add, the last round's too
+// (steps past the range load a valid row and add nothing), so a short K costs a
+// memory latency per round, not one per step.
+//
+// One launch serves several products of the same A (the engine's Q, K and V
+// projections: up to three B / C pairs, their column blocks laid end to end), or
+// the FFN's two input projections with the SwiGLU applied to the reduced sums
+// (out = g / (1 + expf(-g)) * u, the fp32 SwiGLU of src/kernels.cu:185-195 and
+// of bm_swiglu, so the result equals the unfused three launches bit for bit).
 #include <cooperative_groups.h>
 
 #include <algorithm>
@@ -25,99 +35,163 @@ namespace gemm32 {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kCols = 128;     // columns per CTA
+constexpr int kCols = 128;  // columns per CTA
 constexpr int kMaxCluster = 8;
+constexpr int kSteps = 8;   // k steps per warp and round
+constexpr int kShortK = 4 * kSteps * kWarps;  // K per CTA up to which the SHORT form runs
 
 struct Args {
-  float* c;
   const float* a;
-  const float* b;
-  int m, n, k;
-  int k_per_cta;  // K range of one CTA of the cluster
+  const float* b[kMaxSharedA];
+  float* c[kMaxSharedA];
+  int n[kMaxSharedA];
+  int block_end[kMaxSharedA];  // column blocks of outputs 0..o together
+  int count;                   // products of A (SwiGLU: b[0] gate, b[1] up, one output c[0])
+  int m, k;
+  int k_per_cta;               // K range of one CTA of the cluster
 };
 
 // VEC: B rows are 16-byte aligned (N % 4 == 0) and read as float4.
-template <int MT, bool VEC>
+template <bool VEC>
+__device__ __forceinline__ void load_b_row(const float* b, int n, int k, int c0, float (&bv)[4]) {
+  const float* brow = b + static_cast<int64_t>(k) * n;
+  if (VEC) {
+    if (c0 < n) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(brow + c0));
+      bv[0] = v.x;
+      bv[1] = v.y;
+      bv[2] = v.z;
+      bv[3] = v.w;
+    } else {
+      bv[0] = bv[1] = bv[2] = bv[3] = 0.f;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) bv[e] = c0 + e < n ? __ldg(brow + c0 + e) : 0.f;
+  }
+}
+
+// SHORT: each CTA's K range is at most kShortK (the one-token products of small
+// models): loads issued a round at a time, at more registers per thread.
+template <int MT, bool VEC, bool SWIGLU, bool SHORT>
 __global__ void __launch_bounds__(kThreads) gemm_f32_kernel(const Args p) {
-  __shared__ __align__(16) float red[kWarps][MT][kCols];
+  constexpr int kAcc = SWIGLU ? 2 : 1;
+  __shared__ __align__(16) float red[kAcc][kWarps][MT][kCols];
   cg::cluster_group cluster = cg::this_cluster();
   const unsigned ks = cluster.num_blocks(), rank = cluster.block_rank();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int col_block = blockIdx.x / ks;
+  const int gblock = static_cast<int>(blockIdx.x / ks);
+  // this block's output (selected without indexing the parameter arrays, which would copy them to the stack)
+  const int o = SWIGLU ? 0 : (gblock >= p.block_end[0]) + (p.count > 2 && gblock >= p.block_end[1]);
+  const int col_block = gblock - (o == 0 ? 0 : o == 1 ? p.block_end[0] : p.block_end[1]);
+  const int n = o == 0 ? p.n[0] : o == 1 ? p.n[1] : p.n[2];
+  const float* b0 = o == 0 ? p.b[0] : o == 1 ? p.b[1] : p.b[2];
+  const float* b1 = SWIGLU ? p.b[1] : nullptr;
   const int c0 = col_block * kCols + lane * 4;
   const int m0 = blockIdx.y * MT;
   const int kb = static_cast<int>(rank) * p.k_per_cta;
   const int ke = min(p.k, kb + p.k_per_cta);
 
-  float acc[MT][4];
+  float acc[kAcc][MT][4];
 #pragma unroll
-  for (int r = 0; r < MT; ++r)
+  for (int q = 0; q < kAcc; ++q)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) acc[r][e] = 0.f;
+    for (int r = 0; r < MT; ++r)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[q][r][e] = 0.f;
 
   const float* arow[MT];
 #pragma unroll
   for (int r = 0; r < MT; ++r) arow[r] = p.a + static_cast<int64_t>(min(m0 + r, p.m - 1)) * p.k;
 
-  auto step = [&](int k) {
-    float bv[4];
-    const float* brow = p.b + static_cast<int64_t>(k) * p.n;
-    if (VEC) {
-      if (c0 < p.n) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(brow + c0));
-        bv[0] = v.x;
-        bv[1] = v.y;
-        bv[2] = v.z;
-        bv[3] = v.w;
-      } else {
-        bv[0] = bv[1] = bv[2] = bv[3] = 0.f;
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) bv[e] = c0 + e < p.n ? __ldg(brow + c0 + e) : 0.f;
-    }
-#pragma unroll
-    for (int r = 0; r < MT; ++r) {
-      const float av = __ldg(arow[r] + k);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[r][e] = fmaf(av, bv[e], acc[r][e]);
-    }
-  };
-  // warp w takes k = kb + w, kb + w + 8, ...; eight steps' loads in flight together
+  // warp w takes k = kb + w, kb + w + 8, ... in order, kSteps of them per round
   int k = kb + warp;
-  for (; k + 7 * kWarps < ke; k += 8 * kWarps) {
+  if (SHORT) {
+    // a short range (a few rounds): every load of a round is issued before its
+    // first multiply-add, steps past the range loading a valid row and adding nothing
+    for (; k < ke; k += kSteps * kWarps) {
+      float bv[kAcc][kSteps][4], av[kSteps][MT];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) step(k + u * kWarps);
+      for (int u = 0; u < kSteps; ++u) {
+        const int kk = min(k + u * kWarps, ke - 1);
+        load_b_row<VEC>(b0, n, kk, c0, bv[0][u]);
+        if (SWIGLU) load_b_row<VEC>(b1, n, kk, c0, bv[kAcc - 1][u]);
+#pragma unroll
+        for (int r = 0; r < MT; ++r) av[u][r] = __ldg(arow[r] + kk);
+      }
+#pragma unroll
+      for (int u = 0; u < kSteps; ++u) {
+        if (k + u * kWarps < ke) {
+#pragma unroll
+          for (int q = 0; q < kAcc; ++q)
+#pragma unroll
+            for (int r = 0; r < MT; ++r)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) acc[q][r][e] = fmaf(av[u][r], bv[q][u][e], acc[q][r][e]);
+        }
+      }
+    }
+  } else {
+    // a long range: unrolled rounds (the compiler keeps several steps' loads in
+    // flight at the register count of one step), then the remaining steps
+    auto step = [&](int kk) {
+      float bv[kAcc][4];
+      load_b_row<VEC>(b0, n, kk, c0, bv[0]);
+      if (SWIGLU) load_b_row<VEC>(b1, n, kk, c0, bv[kAcc - 1]);
+#pragma unroll
+      for (int r = 0; r < MT; ++r) {
+        const float av = __ldg(arow[r] + kk);
+#pragma unroll
+        for (int q = 0; q < kAcc; ++q)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[q][r][e] = fmaf(av, bv[q][e], acc[q][r][e]);
+      }
+    };
+    for (; k + (kSteps - 1) * kWarps < ke; k += kSteps * kWarps) {
+#pragma unroll
+      for (int u = 0; u < kSteps; ++u) step(k + u * kWarps);
+    }
+    for (; k < ke; k += kWarps) step(k);
   }
-  for (; k < ke; k += kWarps) step(k);
 
 #pragma unroll
-  for (int r = 0; r < MT; ++r)
-    *reinterpret_cast<float4*>(&red[warp][r][lane * 4]) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
-  __syncthreads();
-  // this CTA's partial, summed over its warps, into red[0]
-  for (int i = tid; i < MT * kCols; i += kThreads) {
-    const int r = i / kCols, c = i - r * kCols;
-    float s = red[0][r][c];
+  for (int q = 0; q < kAcc; ++q)
 #pragma unroll
-    for (int w = 1; w < kWarps; ++w) s += red[w][r][c];
-    red[0][r][c] = s;
+    for (int r = 0; r < MT; ++r)
+      *reinterpret_cast<float4*>(&red[q][warp][r][lane * 4]) =
+          make_float4(acc[q][r][0], acc[q][r][1], acc[q][r][2], acc[q][r][3]);
+  __syncthreads();
+  // this CTA's partials, summed over its warps, into red[q][0]
+  for (int i = tid; i < kAcc * MT * kCols; i += kThreads) {
+    const int q = i / (MT * kCols), rc = i - q * (MT * kCols);
+    const int r = rc / kCols, c = rc - r * kCols;
+    float s = red[q][0][r][c];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) s += red[q][w][r][c];
+    red[q][0][r][c] = s;
   }
   cluster.sync();  // every CTA's partial is ready
   if (rank == 0) {
+    float* c_out = o == 0 ? p.c[0] : o == 1 ? p.c[1] : p.c[2];
     for (int i = tid; i < MT * kCols; i += kThreads) {
       const int r = i / kCols, c = i - r * kCols;
-      float s = red[0][r][c];
-      for (unsigned q = 1; q < ks; ++q) s += cluster.map_shared_rank(&red[0][0][0], q)[r * kCols + c];
+      float s = red[0][0][r][c];
+      for (unsigned q = 1; q < ks; ++q) s += cluster.map_shared_rank(&red[0][0][0][0], q)[r * kCols + c];
+      if (SWIGLU) {
+        float u = red[kAcc - 1][0][r][c];
+        for (unsigned q = 1; q < ks; ++q) u += cluster.map_shared_rank(&red[kAcc - 1][0][0][0], q)[r * kCols + c];
+        s = s / (1.0f + expf(-s)) * u;
+      }
       const int row = m0 + r, col = col_block * kCols + c;
-      if (row < p.m && col < p.n) p.c[static_cast<int64_t>(row) * p.n + col] = s;
+      if (row < p.m && col < n) c_out[static_cast<int64_t>(row) * n + col] = s;
     }
   }
   cluster.sync();  // the peers' shared memory stays until the leader has read it
 }
 
-template <int MT>
-int launch_mt(const Args& p, int col_blocks, int row_tiles, int ks, bool vec, cudaStream_t stream) {
+template <int MT, bool SWIGLU>
+int launch_mt(const Args& p, int col_blocks, int row_tiles, int ks, bool vec, cudaStream_t stream,
+              const char* what) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(col_blocks * ks), static_cast<unsigned>(row_tiles), 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -130,38 +204,102 @@ int launch_mt(const Args& p, int col_blocks, int row_tiles, int ks, bool vec, cu
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t err = vec ? cudaLaunchKernelEx(&cfg, gemm_f32_kernel<MT, true>, p)
-                              : cudaLaunchKernelEx(&cfg, gemm_f32_kernel<MT, false>, p);
-  if (err != cudaSuccess) return fail(BM_ERR_CUDA, "bm_gemm (fp32): %s", cudaGetErrorString(err));
-  return check_launch("bm_gemm (fp32)");
+  const bool short_k = p.k_per_cta <= kShortK;
+  cudaError_t err;
+  if (short_k) {
+    err = vec ? cudaLaunchKernelEx(&cfg, gemm_f32_kernel<MT, true, SWIGLU, true>, p)
+              : cudaLaunchKernelEx(&cfg, gemm_f32_kernel<MT, false, SWIGLU, true>, p);
+  } else {
+    err = vec ? cudaLaunchKernelEx(&cfg, gemm_f32_kernel<MT, true, SWIGLU, false>, p)
+              : cudaLaunchKernelEx(&cfg, gemm_f32_kernel<MT, false, SWIGLU, false>, p);
+  }
+  if (err != cudaSuccess) return fail(BM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+  return check_launch(what);
+}
+
+// Plans and launches: the rows in tiles of MT (at most max_mt), the column blocks
+// of every output, and a K split over a cluster until the grid covers the GPU twice.
+template <bool SWIGLU>
+int run(Args p, int64_t m, bool vec, cudaStream_t stream, const char* what) {
+  constexpr int kMaxMt = SWIGLU ? 4 : 8;
+  const int mt = m >= kMaxMt ? kMaxMt : m >= 4 ? 4 : m >= 2 ? 2 : 1;
+  const int64_t row_tiles = (m + mt - 1) / mt;
+  if (row_tiles > 65535) return fail(BM_ERR_INVALID_ARGUMENT, "%s: more than %d rows", what, 65535 * mt);
+  const int col_blocks = p.block_end[p.count - 1];
+  // the K split is chosen for the plain GEMM's tiling (rows in eights), so the
+  // SwiGLU's two products are summed exactly as two bm_gemm calls sum them
+  const int plain_mt = m >= 8 ? 8 : m >= 4 ? 4 : m >= 2 ? 2 : 1;
+  const int64_t base = static_cast<int64_t>(col_blocks) * ((m + plain_mt - 1) / plain_mt);
+  int ks = static_cast<int>(std::min<int64_t>(kMaxCluster, (2 * sm_count() + base - 1) / base));
+  ks = std::max(1, std::min(ks, (p.k + 63) / 64));  // keep >= 64 k per CTA
+  p.m = static_cast<int>(m);
+  p.k_per_cta = (p.k + ks - 1) / ks;
+  const int rt = static_cast<int>(row_tiles);
+  switch (mt) {
+    case 8: return launch_mt<(SWIGLU ? 4 : 8), SWIGLU>(p, col_blocks, rt, ks, vec, stream, what);
+    case 4: return launch_mt<4, SWIGLU>(p, col_blocks, rt, ks, vec, stream, what);
+    case 2: return launch_mt<2, SWIGLU>(p, col_blocks, rt, ks, vec, stream, what);
+    default: return launch_mt<1, SWIGLU>(p, col_blocks, rt, ks, vec, stream, what);
+  }
 }
 
 }  // namespace gemm32
 
-// c[M][N] = a[M][K] b[K][N] in fp32 (host checks done by the caller).
-int gemm_f32(float* c, const float* a, const float* b, int64_t m, int n, int k, cudaStream_t stream) {
+int gemm_f32_shared_a(float* const* c, const float* a, const float* const* b, const int32_t* n, int count,
+                      int64_t m, int k, cudaStream_t stream) {
   using namespace gemm32;
-  if (m == 0 || n == 0) return BM_OK;
-  if (k == 0) {  // an empty sum
-    const cudaError_t err = cudaMemsetAsync(c, 0, static_cast<size_t>(m) * n * sizeof(float), stream);
-    return err == cudaSuccess ? BM_OK : fail(BM_ERR_CUDA, "bm_gemm (fp32): %s", cudaGetErrorString(err));
+  const char* what = "bm_gemm (fp32)";
+  if (m == 0) return BM_OK;
+  Args p{};
+  p.a = a;
+  p.k = k;
+  bool vec = true;
+  int blocks = 0, live = 0;
+  for (int o = 0; o < count; ++o) {
+    if (n[o] == 0) continue;  // an empty product: nothing to write
+    if (k == 0) {             // an empty sum
+      const cudaError_t err = cudaMemsetAsync(c[o], 0, static_cast<size_t>(m) * n[o] * sizeof(float), stream);
+      if (err != cudaSuccess) return fail(BM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+      continue;
+    }
+    p.b[live] = b[o];
+    p.c[live] = c[o];
+    p.n[live] = n[o];
+    blocks += (n[o] + kCols - 1) / kCols;
+    p.block_end[live] = blocks;
+    vec = vec && n[o] % 4 == 0 && aligned16(b[o]);
+    ++live;
   }
-  const int mt = m >= 8 ? 8 : m >= 4 ? 4 : m >= 2 ? 2 : 1;
-  const int64_t row_tiles = (m + mt - 1) / mt;
-  if (row_tiles > 65535) return fail(BM_ERR_INVALID_ARGUMENT, "bm_gemm (fp32): more than %d rows", 65535 * 8);
-  const int col_blocks = (n + kCols - 1) / kCols;
-  // split K over a cluster until the grid covers the GPU twice, keeping >= 64 k per CTA
-  const int64_t base = static_cast<int64_t>(col_blocks) * row_tiles;
-  int ks = static_cast<int>(std::min<int64_t>(kMaxCluster, (2 * sm_count() + base - 1) / base));
-  ks = std::max(1, std::min(ks, (k + 63) / 64));
-  Args p{c, a, b, static_cast<int>(m), n, k, (k + ks - 1) / ks};
-  const bool vec = n % 4 == 0 && aligned16(b);
-  switch (mt) {
-    case 8: return launch_mt<8>(p, col_blocks, static_cast<int>(row_tiles), ks, vec, stream);
-    case 4: return launch_mt<4>(p, col_blocks, static_cast<int>(row_tiles), ks, vec, stream);
-    case 2: return launch_mt<2>(p, col_blocks, static_cast<int>(row_tiles), ks, vec, stream);
-    default: return launch_mt<1>(p, col_blocks, static_cast<int>(row_tiles), ks, vec, stream);
+  if (live == 0) return BM_OK;
+  p.count = live;
+  return run<false>(p, m, vec, stream, what);
+}
+
+int gemm_f32(float* c, const float* a, const float* b, int64_t m, int n, int k, cudaStream_t stream) {
+  const int32_t n32 = n;
+  return gemm_f32_shared_a(&c, a, &b, &n32, 1, m, k, stream);
+}
+
+int gemm_f32_swiglu(float* out, const float* x, const float* w_gate, const float* w_up, int64_t rows, int hidden,
+                    int dim, cudaStream_t stream) {
+  using namespace gemm32;
+  const char* what = "bm_gemm_swiglu (fp32)";
+  if (rows == 0 || hidden == 0) return BM_OK;
+  if (dim == 0) {  // both sums are empty: silu(0) * 0 = 0
+    const cudaError_t err = cudaMemsetAsync(out, 0, static_cast<size_t>(rows) * hidden * sizeof(float), stream);
+    return err == cudaSuccess ? BM_OK : fail(BM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
   }
+  Args p{};
+  p.a = x;
+  p.k = dim;
+  p.b[0] = w_gate;
+  p.b[1] = w_up;
+  p.c[0] = out;
+  p.n[0] = p.n[1] = hidden;
+  p.block_end[0] = (hidden + kCols - 1) / kCols;
+  p.count = 1;
+  const bool vec = hidden % 4 == 0 && aligned16(w_gate) && aligned16(w_up);
+  return run<true>(p, rows, vec, stream, what);
 }
 
 }  // namespace bm

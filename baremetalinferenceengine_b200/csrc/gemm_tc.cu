@@ -563,6 +563,15 @@ extern "C" int bm_gemm_swiglu(void* out, const void* x, const void* w_gate, cons
                               int32_t dim, int32_t hidden, bm_dtype_t dtype, int32_t* d_status, void* stream) {
   using namespace bm;
   const char* what = "bm_gemm_swiglu";
+  if (dtype == BM_F32) {  // fp32 operands: CUDA cores, any shape (gemm_f32.cu)
+    if (rows < 0 || rows > (int64_t{1} << 31) || dim < 0 || hidden < 0) {
+      return fail(BM_ERR_INVALID_ARGUMENT, "%s: negative or too large size", what);
+    }
+    if (rows == 0 || hidden == 0) return BM_OK;
+    if (!out || (dim > 0 && (!x || !w_gate || !w_up))) return fail(BM_ERR_INVALID_ARGUMENT, "%s: NULL pointer", what);
+    return gemm_f32_swiglu(static_cast<float*>(out), static_cast<const float*>(x), static_cast<const float*>(w_gate),
+                           static_cast<const float*>(w_up), rows, hidden, dim, as_stream(stream));
+  }
   if (int st = gemm::check_shapes(what, rows, hidden, dim, dtype)) return st;
   return gemm::run<true>(what, out, x, w_gate, w_up, rows, hidden, dim, d_status, stream);
 }
@@ -582,4 +591,30 @@ extern "C" int bm_gemm(void* c, const void* a, const void* b, int64_t m, int32_t
   }
   if (int st = gemm::check_shapes(what, m, n, k, dtype)) return st;
   return gemm::run<false>(what, c, a, b, b, m, n, k, d_status, stream);
+}
+
+extern "C" int bm_gemm_shared_a(void* const* c, const void* a, const void* const* b, const int32_t* n,
+                                int32_t count, int64_t m, int32_t k, bm_dtype_t dtype, int32_t* d_status,
+                                void* stream) {
+  using namespace bm;
+  const char* what = "bm_gemm_shared_a";
+  if (count < 1 || count > kMaxSharedA) return fail(BM_ERR_INVALID_ARGUMENT, "%s: count outside [1, 3]", what);
+  if (!c || !b || !n) return fail(BM_ERR_INVALID_ARGUMENT, "%s: NULL array", what);
+  if (m < 0 || m > (int64_t{1} << 31) || k < 0) return fail(BM_ERR_INVALID_ARGUMENT, "%s: negative or too large size", what);
+  for (int o = 0; o < count; ++o) {
+    if (n[o] < 0) return fail(BM_ERR_INVALID_ARGUMENT, "%s: negative width", what);
+    if (m > 0 && n[o] > 0 && (!c[o] || (k > 0 && (!a || !b[o])))) {
+      return fail(BM_ERR_INVALID_ARGUMENT, "%s: NULL pointer", what);
+    }
+  }
+  if (dtype == BM_F32) {
+    return gemm_f32_shared_a(reinterpret_cast<float* const*>(c), static_cast<const float*>(a),
+                             reinterpret_cast<const float* const*>(b), n, count, m, k, as_stream(stream));
+  }
+  if (dtype != BM_BF16) return fail(BM_ERR_INVALID_ARGUMENT, "%s: bad dtype", what);
+  for (int o = 0; o < count; ++o) {
+    if (m == 0 || n[o] == 0) continue;  // an empty product: nothing to write
+    if (int st = bm_gemm(c[o], a, b[o], m, n[o], k, dtype, d_status, stream)) return st;
+  }
+  return BM_OK;
 }

@@ -70,8 +70,6 @@ void ExecutionEngine::reserve(int tokens) {
   v_ = buffer(n * dim);
   attention_out_ = buffer(n * dim);
   projected_ = buffer(n * dim);
-  gate_ = buffer(n * hidden);
-  up_ = buffer(n * hidden);
   activated_ = buffer(n * hidden);
   ids_ = std::make_shared<DeviceBuffer<int>>(n);
   positions_ = std::make_shared<DeviceBuffer<int>>(n);
@@ -180,9 +178,14 @@ void ExecutionEngine::run(int T, int max_len) {
       check(bm_add_rmsnorm(hidden_, projected_, w.attention_norm, normed_, T, dim, eps, BM_F32, stream_),
             "bm_add_rmsnorm");
     }
-    launch_gemm(q_, normed_, w.q_proj, T, dim, dim, stream_);
-    launch_gemm(k_, normed_, w.k_proj, T, dim, dim, stream_);
-    launch_gemm(v_, normed_, w.v_proj, T, dim, dim, stream_);
+    // Q, K and V projections of the same normed rows: one launch
+    {
+      void* outs[3] = {q_, k_, v_};
+      const void* weights[3] = {w.q_proj, w.k_proj, w.v_proj};
+      const int32_t widths[3] = {dim, dim, dim};
+      check(bm_gemm_shared_a(outs, normed_, weights, widths, 3, T, dim, BM_F32, nullptr, stream_),
+            "bm_gemm_shared_a");
+    }
     // Token t at cache position positions_[t] of the one sequence the reference's cache holds.
     check(bm_rope_kv_store(q_, k_, v_, positions_->get(), 0, nullptr, k_cache, v_cache, rope_table_->get(),
                            max_seq, config_.rope_theta, T, heads, heads, head_dim, max_seq, 1, BM_F32, nullptr,
@@ -195,9 +198,9 @@ void ExecutionEngine::run(int T, int max_len) {
           "bm_decode_attention");
     launch_gemm(projected_, attention_out_, w.o_proj, T, dim, dim, stream_);
     check(bm_add_rmsnorm(hidden_, projected_, w.ffn_norm, normed_, T, dim, eps, BM_F32, stream_), "bm_add_rmsnorm");
-    launch_gemm(gate_, normed_, w.gate_proj, T, hidden_dim, dim, stream_);
-    launch_gemm(up_, normed_, w.up_proj, T, hidden_dim, dim, stream_);
-    check(bm_swiglu(activated_, gate_, up_, static_cast<int64_t>(T) * hidden_dim, BM_F32, stream_), "bm_swiglu");
+    // gate and up projections with the SwiGLU in the epilogue (:122-124): one launch
+    check(bm_gemm_swiglu(activated_, normed_, w.gate_proj, w.up_proj, T, dim, hidden_dim, BM_F32, nullptr, stream_),
+          "bm_gemm_swiglu");
     launch_gemm(projected_, activated_, w.down_proj, T, dim, hidden_dim, stream_);
   }
 

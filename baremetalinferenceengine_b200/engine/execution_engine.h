@@ -13,7 +13,9 @@
 //     embedding gather, the residual add fused into the RMSNorm that follows it
 //     (:118+:121, :126+:109, :126+:80), RoPE fused with both KV-cache writes
 //     (:113-115), and the split decode attention (:116).
-// The projections use this library's fp32 launch_gemm. Every launch goes to the
+// The projections are this library's fp32 GEMMs: Q, K and V in one launch
+// (bm_gemm_shared_a), the gate and up projections with the SwiGLU in their
+// epilogue (bm_gemm_swiglu, :122-124), the others through launch_gemm. Every launch goes to the
 // engine's own stream, and a one-token forward (a decode step) replays a CUDA
 // graph of the whole layer loop, captured on the second such call: positions and
 // attended lengths come from small device arrays refreshed before each replay,
@@ -85,8 +87,6 @@ class ExecutionEngine {
   float* v_ = nullptr;
   float* attention_out_ = nullptr;
   float* projected_ = nullptr;
-  float* gate_ = nullptr;
-  float* up_ = nullptr;
   float* activated_ = nullptr;
   std::shared_ptr<DeviceBuffer<int>> ids_;
   // Every layer and the logits of the last token for T tokens on stream_;

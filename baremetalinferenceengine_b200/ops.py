@@ -195,8 +195,9 @@ def add(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, st
 
 def gemm_swiglu(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, out: Optional[torch.Tensor] = None,
                 status: Optional[DeviceStatus] = None, stream=None) -> torch.Tensor:
-    """out = silu(x @ w_gate) * (x @ w_up) on the tensor cores (bf16): x [rows, dim],
-    w_gate and w_up [dim, hidden] (the reference's [in][out] weight layout)."""
+    """out = silu(x @ w_gate) * (x @ w_up): x [rows, dim], w_gate and w_up [dim, hidden]
+    (the reference's [in][out] weight layout). bf16 on the tensor cores; fp32 on CUDA
+    cores (the SwiGLU of bm_swiglu applied to the reduced products)."""
     for t, name in ((x, "x"), (w_gate, "w_gate"), (w_up, "w_up")):
         _dense(t, name)
     if x.dim() != 2 or w_gate.dim() != 2 or w_gate.shape != w_up.shape or w_gate.shape[0] != x.shape[1]:
@@ -235,6 +236,38 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None,
         check(load().bm_gemm(_ptr(out), _ptr(a), _ptr(b), m, n, k, bm_dtype(a), status.ptr if status else None,
                              _stream(a.device, stream)))
     return out
+
+
+def gemm_shared_a(a: torch.Tensor, bs, outs=None, status: Optional[DeviceStatus] = None, stream=None):
+    """[a @ b for b in bs] for one to three weights b [k, n_o] (an attention block's Q,
+    K and V projections): fp32 in one launch, bf16 one tensor-core GEMM per weight."""
+    _dense(a, "a")
+    bs = list(bs)
+    if not 1 <= len(bs) <= 3:
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "one to three weights")
+    if a.dim() != 2:
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "need a [m, k]")
+    m, k = a.shape
+    for b in bs:
+        _dense(b, "b")
+        if b.dim() != 2 or b.shape[0] != k:
+            raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "need every b [k, n]")
+    if outs is None:
+        outs = [torch.empty((m, b.shape[1]), dtype=a.dtype, device=a.device) for b in bs]
+    outs = list(outs)
+    for b, out in zip(bs, outs):
+        _dense(out, "out")
+        if tuple(out.shape) != (m, b.shape[1]):
+            raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "every out must be [m, n]")
+    _same(a, *bs, *outs)
+    count = len(bs)
+    c_arr = (ctypes.c_void_p * count)(*[_ptr(o) for o in outs])
+    b_arr = (ctypes.c_void_p * count)(*[_ptr(b) for b in bs])
+    n_arr = (ctypes.c_int32 * count)(*[b.shape[1] for b in bs])
+    with torch.cuda.device(_dev(a)):
+        check(load().bm_gemm_shared_a(c_arr, _ptr(a), b_arr, n_arr, count, m, k, bm_dtype(a),
+                                      status.ptr if status else None, _stream(a.device, stream)))
+    return outs
 
 
 def softmax(x: torch.Tensor, size: Optional[int] = None, num_vectors: int = 1, stride: Optional[int] = None,

@@ -232,8 +232,9 @@ int bm_decode_attention_static_scratch(void* out, const void* q, const void* k_c
  * Tensor-core GEMMs (tcgen05, bf16 operands, fp32 accumulation, bf16 output).
  * The activation is [rows][K] row-major; weights are [K][N] row-major, the
  * layout of launch_gemm's B operand (include/kernels.cuh:20, src/kernels.cu:83-121).
- * N and K must be multiples of 8 and every pointer 16-byte aligned; any row
- * count. BM_F32 is rejected (the tensor-core path takes bf16).
+ * For BM_BF16: N and K multiples of 8, every pointer 16-byte aligned, any row
+ * count (tcgen05). BM_F32 (any shape, no alignment needed) runs on CUDA cores in
+ * fp32 (below).
  *
  * bm_gemm_swiglu: out[r][f] = silu(sum_d x[r][d] w_gate[d][f]) * sum_d x[r][d] w_up[d][f]
  * for x [rows][dim], w_gate and w_up [dim][hidden], out [rows][hidden]: the two
@@ -241,14 +242,23 @@ int bm_decode_attention_static_scratch(void* out, const void* q, const void* k_c
  * kernel, the products kept in fp32 until the SwiGLU. bm_gemm: c[M][N] = a[M][K] b[K][N].
  * A pipeline wait that passes its time limit (a fault, never a slow input) sets
  * BM_DEVERR_TIMEOUT in *d_status.
- * bm_gemm also takes BM_F32 (any M, N, K; no alignment needed): fp32 arithmetic on
- * CUDA cores, built for few rows (the reference engine's one-token products,
- * src/execution_engine.cu:81,110-125), K split over a thread-block cluster and
- * reduced in a fixed order (deterministic); d_status is not used. */
+ * BM_F32: fp32 arithmetic on CUDA cores, built for few rows (the reference
+ * engine's one-token products, src/execution_engine.cu:81,110-125), K split over a
+ * thread-block cluster and reduced in a fixed order (deterministic); d_status is
+ * not used. bm_gemm_swiglu's fp32 SwiGLU is g / (1 + expf(-g)) * u, as bm_swiglu,
+ * so it equals bm_gemm twice and bm_swiglu bit for bit.
+ *
+ * bm_gemm_shared_a: c[o] = a . b[o] for o < count (1 to 3), the products of one
+ * activation with several weights (an attention block's Q, K and V projections):
+ * c, b and n are host arrays of count device pointers and widths, a is [m][k],
+ * b[o] [k][n[o]], c[o] [m][n[o]]. BM_F32 runs all of them in one launch; BM_BF16
+ * runs bm_gemm once per product. */
 int bm_gemm_swiglu(void* out, const void* x, const void* w_gate, const void* w_up, int64_t rows, int32_t dim,
                    int32_t hidden, bm_dtype_t dtype, int32_t* d_status, void* stream);
 int bm_gemm(void* c, const void* a, const void* b, int64_t m, int32_t n, int32_t k, bm_dtype_t dtype,
             int32_t* d_status, void* stream);
+int bm_gemm_shared_a(void* const* c, const void* a, const void* const* b, const int32_t* n, int32_t count,
+                     int64_t m, int32_t k, bm_dtype_t dtype, int32_t* d_status, void* stream);
 
 /* Softmax in place over num_vectors vectors of `size` elements, `stride`
  * elements apart (the gaps untouched): x = exp(x - max) / sum exp(x - max), fp32

@@ -87,6 +87,9 @@ def test_abi_version_and_status_strings(lib):
 
 
 FAKE = 0x100000  # never dereferenced: every call below fails or returns before any CUDA call
+PTRS3 = (ctypes.c_void_p * 3)(FAKE, FAKE, FAKE)  # host arrays of (fake) device pointers
+WIDTHS3 = (ctypes.c_int32 * 3)(8, 8, 8)
+WIDTHS_BAD = (ctypes.c_int32 * 3)(8, -1, 8)
 
 
 @pytest.mark.parametrize("call", [
@@ -133,7 +136,8 @@ FAKE = 0x100000  # never dereferenced: every call below fails or returns before 
     lambda L: L.bm_gemm(FAKE, FAKE, FAKE, -1, 64, 64, 1, None, None),                 # negative rows
     lambda L: L.bm_gemm(FAKE, FAKE + 2, FAKE, 4, 64, 64, 1, None, None),              # misaligned operand
     lambda L: L.bm_gemm(FAKE, None, FAKE, 4, 64, 64, 1, None, None),                  # NULL operand
-    lambda L: L.bm_gemm_swiglu(FAKE, FAKE, FAKE, FAKE, 4, 64, 64, 0, None, None),    # fp32
+    lambda L: L.bm_gemm_swiglu(FAKE, FAKE, FAKE, FAKE, -4, 64, 64, 0, None, None),   # fp32: negative rows
+    lambda L: L.bm_gemm_swiglu(FAKE, FAKE, None, FAKE, 4, 64, 64, 0, None, None),    # fp32: NULL w_gate
     lambda L: L.bm_gemm_swiglu(FAKE, FAKE, FAKE, FAKE, 4, 64, 60, 1, None, None),    # hidden % 8
     lambda L: L.bm_gemm_swiglu(FAKE, FAKE, FAKE, None, 4, 64, 64, 1, None, None),    # NULL w_up
     lambda L: L.bm_gemm(FAKE, None, FAKE, 4, 5, 7, 0, None, None),                    # fp32: NULL operand
@@ -142,6 +146,12 @@ FAKE = 0x100000  # never dereferenced: every call below fails or returns before 
     lambda L: L.bm_softmax(FAKE, -1, 1, 8, 0, None),                                  # negative size
     lambda L: L.bm_softmax(None, 8, 1, 8, 0, None),                                   # NULL x
     lambda L: L.bm_softmax(FAKE, 8, 1, 8, 9, None),                                   # bad dtype
+    lambda L: L.bm_gemm_shared_a(None, FAKE, None, None, 1, 4, 8, 0, None, None),    # NULL arrays
+    lambda L: L.bm_gemm_shared_a(PTRS3, FAKE, PTRS3, WIDTHS_BAD, 3, 4, 8, 0, None, None),  # negative width
+    lambda L: L.bm_gemm_shared_a(PTRS3, FAKE, PTRS3, WIDTHS3, 0, 4, 8, 0, None, None),     # count 0
+    lambda L: L.bm_gemm_shared_a(PTRS3, FAKE, PTRS3, WIDTHS3, 4, 4, 8, 0, None, None),     # count 4
+    lambda L: L.bm_gemm_shared_a(PTRS3, None, PTRS3, WIDTHS3, 3, 4, 8, 0, None, None),     # NULL a
+    lambda L: L.bm_gemm_shared_a(PTRS3, FAKE, PTRS3, WIDTHS3, 3, 4, 8, 9, None, None),     # bad dtype
     lambda L: L.bm_selftest_bounded_wait(1000, FAKE, FAKE, None),                     # limit below 1 ms
     lambda L: L.bm_selftest_bounded_wait(10**10, FAKE, FAKE, None),                   # limit above 2 s
     lambda L: L.bm_selftest_bounded_wait(50 * 10**6, None, FAKE, None),               # NULL status

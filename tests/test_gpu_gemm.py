@@ -169,6 +169,56 @@ def test_fp32_gemm_misaligned_operands(cuda):
     assert orc.worst_error(c.cpu().numpy(), want) <= 1e-5
 
 
+@pytest.mark.parametrize("rows,dim,hidden", [
+    (1, 288, 768), (48, 288, 768),         # the engine's FFN: one token, and a 48-token prompt
+    (5, 7, 13), (9, 130, 200), (1, 4096, 14336),  # ragged shapes (hidden % 4 != 0: scalar loads), long rows
+    (64, 512, 1000),                        # many rows: the SwiGLU tiles 4 rows, the plain GEMM 8
+])
+def test_fp32_gemm_swiglu_matches_the_oracle_and_the_unfused_ops(cuda, rows, dim, hidden):
+    """bm_gemm_swiglu in fp32: within 1e-5 of the oracle (silu(x Wg) * (x Wu) in double),
+    and bit-identical to bm_gemm twice followed by bm_swiglu. Weights at the scale of a
+    model's (about 1/sqrt(dim)), so the products stay O(1) at every K."""
+    g = gen(rows * 7 + dim + hidden)
+    x = (torch.rand(rows, dim, generator=g) * 2 - 1)
+    scale = 2.0 / dim ** 0.5
+    wg = (torch.rand(dim, hidden, generator=g) * 2 - 1) * scale
+    wu = (torch.rand(dim, hidden, generator=g) * 2 - 1) * scale
+    xd, wgd, wud = x.to(cuda), wg.to(cuda), wu.to(cuda)
+    out = ops.gemm_swiglu(xd, wgd, wud)
+    unfused = ops.swiglu(ops.gemm(xd, wgd), ops.gemm(xd, wud))
+    torch.cuda.synchronize(cuda)
+    want = orc.gemm_swiglu(x.numpy(), wg.numpy(), wu.numpy(), threads=8)
+    assert orc.worst_error(out.cpu().numpy(), want) <= 1e-5
+    assert bits_equal(out, unfused)
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("m,k,widths", [
+    (1, 288, (288, 288, 288)),      # the engine's Q, K and V (heads = kv heads)
+    (1, 4096, (4096, 1024, 1024)),  # Llama-3-8B Q, K, V (GQA)
+    (48, 288, (288, 96, 96)),       # a prompt of 48 tokens, GQA widths
+    (3, 64, (40, 0, 24)),           # an empty product between two others
+    (2, 256, (128,)),               # one product
+])
+def test_shared_a_products_match_the_oracle(cuda, dt, m, k, widths):
+    """bm_gemm_shared_a: each c[o] = a . b[o] within the GEMM tolerance of its dtype;
+    fp32 runs all products in one launch."""
+    if dt == torch.bfloat16 and any(w % 8 for w in widths):
+        pytest.skip("bf16 widths are multiples of 8")
+    g = gen(m + k + sum(widths))
+    a = torch.rand(m, k, generator=g) * 2 - 1
+    bs = [(torch.rand(k, w, generator=g) * 2 - 1) * 0.2 for w in widths]
+    outs = ops.gemm_shared_a(a.to(cuda).to(dt), [b.to(cuda).to(dt) for b in bs])
+    torch.cuda.synchronize(cuda)
+    tol = 1e-5 if dt == torch.float32 else BF16_TOL
+    for b, out in zip(bs, outs):
+        assert out.shape == (m, b.shape[1])
+        if b.shape[1] == 0:
+            continue
+        want = orc.gemm(to_np(a.to(dt)), to_np(b.to(dt)), threads=8)
+        assert orc.worst_error(to_np(out), want) <= tol
+
+
 @pytest.mark.parametrize("size,vectors,stride,lo,hi", [
     (1, 1, 1, -4, 4), (100, 1, 100, -4, 4), (4096, 1, 4096, -4, 4),   # tests/kernel_tests.cu:268-275
     (1000, 1, 1000, 995, 1005),                                         # values near 1000 (:140-147)
