@@ -35,6 +35,9 @@ namespace attn {
 #endif
 // Splits of the TMA-fed kernels hold at least this many 128-position tiles.
 constexpr int kStagedMinTiles = BM_ATTN_STAGED_MIN_TILES;
+// Splits of the CUDA-core kernel hold at least two: a sequence of one or two tiles
+// runs whole in one CTA rather than paying a second launch to merge its halves.
+constexpr int kCudaCoreMinTiles = 2;
 
 // min_tiles: the fewest tiles a split may hold (the tensor-core kernel pays a
 // fixed start-up per CTA, so its splits keep at least four tiles).
@@ -117,7 +120,7 @@ int decode_attention(void* out, const void* q, const void* k_cache, const void* 
     }
   }
   plan_splits(batch * hkv, max_len, sm_count(), &a.splits, &a.split_len,
-              tc || f32_tma_eligible(a, dtype) ? kStagedMinTiles : 1);
+              tc || f32_tma_eligible(a, dtype) ? kStagedMinTiles : kCudaCoreMinTiles);
   const size_t need = workspace_bytes(batch, hkv, a.group, hd, a.splits);
   if (need > 0 && (workspace == nullptr || workspace_size < need)) {
     // Less scratch than the plan wants: as many splits as it holds (maybe one).
