@@ -78,6 +78,7 @@ template <int GM>
 __global__ void __launch_bounds__(kFThreads, 1)
     attention_f32_tma_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                              const AttnArgs a) {
+  grid_dependency_wait();
   const int64_t b = blockIdx.z;
   const int kvh = blockIdx.y;
   const int split = blockIdx.x;
@@ -318,7 +319,10 @@ int launch_f32_tma(const AttnArgs& a, cudaStream_t stream) {
   const dim3 grid(a.splits, a.hkv, static_cast<unsigned>(a.batch));
   auto go = [&](auto kernel) {
     if (int st = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), kFSmemBytes, what)) return st;
-    kernel<<<grid, kFThreads, kFSmemBytes, stream>>>(tk, tv, a);
+    if (const int launch_status = launch_kernel(what, kernel, dim3(grid), dim3(kFThreads), kFSmemBytes, stream,
+                                                nullptr, tk, tv, a)) {
+      return launch_status;
+    }
     return check_launch(what);
   };
   int st;

@@ -118,6 +118,7 @@ __device__ __forceinline__ void load_n(const T* p, float* f) {
 // and reads them with one vector load; otherwise it owns l, l + 32, ...
 template <typename T, int GM, int DPL, bool CONTIG>
 __global__ void __launch_bounds__(kThreads) attention_split_kernel(AttnArgs a) {
+  grid_dependency_wait();
   constexpr int VEC = VecWidth<T>::value;
   constexpr int KCHUNKS = (32 * DPL + VEC - 1) / VEC;  // 16-byte chunks of the longest K row
   constexpr int KB = KCHUNKS < 8 ? KCHUNKS : 8;           // chunks loaded together
@@ -338,6 +339,7 @@ __device__ __forceinline__ float combine_block_reduce(float v, bool is_max, floa
 
 template <typename T>
 __global__ void __launch_bounds__(kCombineThreads) attention_combine_kernel(AttnArgs a) {
+  grid_dependency_wait();
   extern __shared__ float w_s[];  // [splits]
   __shared__ float red[kCombineThreads / 32];
   const int64_t b = blockIdx.y;
@@ -376,8 +378,11 @@ __global__ void __launch_bounds__(kCombineThreads) attention_combine_kernel(Attn
 // Launches the combine step for a split plan.
 template <typename T>
 int launch_combine(const AttnArgs& a, cudaStream_t stream) {
-  attention_combine_kernel<T><<<dim3(a.hq, static_cast<unsigned>(a.batch)), kCombineThreads,
-                                static_cast<size_t>(a.splits) * sizeof(float), stream>>>(a);
+  if (const int launch_status = launch_kernel("attention_combine_kernel", attention_combine_kernel<T>,
+                                              dim3(dim3(a.hq, static_cast<unsigned>(a.batch))), dim3(kCombineThreads),
+                                              static_cast<size_t>(a.splits) * sizeof(float), stream, nullptr, a)) {
+    return launch_status;
+  }
   return check_launch("bm_decode_attention (combine)");
 }
 
@@ -393,7 +398,10 @@ int launch_group(const AttnArgs& a, size_t smem, cudaStream_t stream) {
         return st;
       }
     }
-    kernel<<<grid, kThreads, smem, stream>>>(a);
+    if (const int launch_status =
+            launch_kernel("bm_decode_attention", kernel, dim3(grid), dim3(kThreads), smem, stream, nullptr, a)) {
+      return launch_status;
+    }
     return check_launch("bm_decode_attention");
   };
   const int dpl = (a.hd + 31) / 32;

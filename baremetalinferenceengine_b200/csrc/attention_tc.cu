@@ -96,6 +96,7 @@ template <int GM>
 __global__ void __launch_bounds__(kTcThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                         const AttnArgs a) {
+  grid_dependency_wait();
   const int64_t b = blockIdx.z;
   const int kvh = blockIdx.y;
   const int split = blockIdx.x;
@@ -384,7 +385,10 @@ int launch_tc(const AttnArgs& a, cudaStream_t stream) {
   const dim3 grid(a.splits, a.hkv, static_cast<unsigned>(a.batch));
   auto go = [&](auto kernel) {
     if (int st = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), kTcSmemBytes, what)) return st;
-    kernel<<<grid, kTcThreads, kTcSmemBytes, stream>>>(tk, tv, a);
+    if (const int launch_status = launch_kernel(what, kernel, dim3(grid), dim3(kTcThreads), kTcSmemBytes, stream,
+                                                nullptr, tk, tv, a)) {
+      return launch_status;
+    }
     return check_launch(what);
   };
   int st;

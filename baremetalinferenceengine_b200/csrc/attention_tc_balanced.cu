@@ -162,6 +162,7 @@ template <int GM>
 __global__ void __launch_bounds__(kThreadsB, 1)
     attention_tc_balanced_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                                  const __grid_constant__ CUtensorMap tq, const AttnArgs a) {
+  grid_dependency_wait();
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                          ~static_cast<uintptr_t>(1023));
@@ -496,6 +497,7 @@ __global__ void __launch_bounds__(kThreadsB, 1)
 // One CTA per (query of a group, CTA of the main kernel): when that CTA recorded
 // a pair split across CTAs, merges the pair's partials for that query.
 __global__ void __launch_bounds__(kCombineThreads) balanced_combine_kernel(const AttnArgs a) {
+  grid_dependency_wait();
   extern __shared__ float w_s[];  // [pieces]
   __shared__ float red[kCombineThreads / 32];
   const int g = blockIdx.x, k = blockIdx.y, nc = a.splits;
@@ -568,7 +570,10 @@ int launch_tc_balanced(AttnArgs a, int ctas, cudaStream_t stream) {
   a.splits = ctas;  // the combine step reads the CTA count from here
   auto go = [&](auto kernel) {
     if (int st = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), kSmemBytes, what)) return st;
-    kernel<<<ctas, kThreadsB, kSmemBytes, stream>>>(tk, tv, tq, a);
+    if (const int launch_status = launch_kernel(what, kernel, dim3(ctas), dim3(kThreadsB), kSmemBytes, stream,
+                                                nullptr, tk, tv, tq, a)) {
+      return launch_status;
+    }
     return check_launch(what);
   };
   int st;
@@ -584,8 +589,11 @@ int launch_tc_balanced(AttnArgs a, int ctas, cudaStream_t stream) {
     st = go(attention_tc_balanced_kernel<16>);
   }
   if (st != BM_OK) return st;
-  balanced_combine_kernel<<<dim3(a.group, ctas), kCombineThreads, static_cast<size_t>(ctas) * sizeof(float),
-                            stream>>>(a);
+  if (const int launch_status = launch_kernel("balanced_combine_kernel", balanced_combine_kernel,
+                                              dim3(dim3(a.group, ctas)), dim3(kCombineThreads),
+                                              static_cast<size_t>(ctas) * sizeof(float), stream, nullptr, a)) {
+    return launch_status;
+  }
   return check_launch("bm_decode_attention (combine)");
 }
 

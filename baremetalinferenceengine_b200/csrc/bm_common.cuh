@@ -129,4 +129,10 @@ __device__ __forceinline__ void raise_status(int32_t* status, int32_t bits) {
   if (status != nullptr) atomicOr(status, bits);
 }
 
+// First statement of every kernel of this library: with programmatic dependent
+// launch (launch_kernel), a kernel may start while the one before it on the stream
+// is finishing; this waits until that kernel has completed and its writes are
+// visible, before any read or write of memory. A no-op for a normal launch.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 }  // namespace bm

@@ -18,6 +18,38 @@ void clear_error();
 // Returns BM_OK, or BM_ERR_CUDA with the launch error of `what` recorded.
 int check_launch(const char* what);
 
+// Programmatic dependent launch for this library's kernels: on unless the
+// environment sets BM_PDL=0 (read once).
+bool pdl_enabled();
+
+// Launches `kernel` with programmatic stream serialization when pdl_enabled():
+// its blocks may be scheduled while the previous kernel on the stream finishes,
+// and it waits for that kernel (grid_dependency_wait) before touching memory, so
+// launch latency overlaps the previous kernel's tail, also inside CUDA graphs.
+// extra_attr (optional) is one more launch attribute (a cluster shape).
+template <typename... KArgs, typename... Args>
+int launch_kernel(const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                  cudaStream_t stream, const cudaLaunchAttribute* extra_attr, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (extra_attr != nullptr) attr[n++] = *extra_attr;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  if (err != cudaSuccess) return fail(BM_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(err));
+  return check_launch(what);
+}
+
 // Streaming multiprocessors of the current device (cached per device).
 int sm_count();
 

@@ -2,6 +2,8 @@
 // read-back and per-device SM counts.
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 
 #include <map>
 #include <mutex>
@@ -26,6 +28,14 @@ int fail(int status, const char* fmt, ...) {
 }
 
 void clear_error() { g_message[0] = '\0'; }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("BM_PDL");
+    return v == nullptr || std::strcmp(v, "0") != 0;
+  }();
+  return on;
+}
 
 int check_launch(const char* what) {
   cudaError_t err = cudaGetLastError();

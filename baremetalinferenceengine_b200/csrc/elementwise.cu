@@ -60,6 +60,7 @@ __device__ __forceinline__ float apply(float a, float b) {
 template <typename T, Op OP>
 __global__ void __launch_bounds__(kThreads, BM_EW_MINB) binary_vec_kernel(T* out, const T* a, const T* b,
                                                              int64_t n) {
+  grid_dependency_wait();
   constexpr int N = VecWidth<T>::value;
   const int64_t nvec = n / N;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
@@ -97,6 +98,7 @@ __global__ void __launch_bounds__(kThreads, BM_EW_MINB) binary_vec_kernel(T* out
 
 template <typename T, Op OP>
 __global__ void __launch_bounds__(kThreads) binary_scalar_kernel(T* out, const T* a, const T* b, int64_t n) {
+  grid_dependency_wait();
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n; i += stride) {
     store1<T>(out + i, apply<T, OP>(load1<T>(a + i), load1<T>(b + i)));
@@ -111,13 +113,19 @@ int launch(void* out, const void* a, const void* b, int64_t n, cudaStream_t stre
     const int64_t nvec = n / N;
     const int64_t need = std::max<int64_t>(1, (nvec + kThreads * kUnroll - 1) / (kThreads * kUnroll));
     const unsigned grid = static_cast<unsigned>(std::min(need, cap));
-    binary_vec_kernel<T, OP><<<grid, kThreads, 0, stream>>>(static_cast<T*>(out), static_cast<const T*>(a),
-                                                           static_cast<const T*>(b), n);
+    if (const int launch_status = launch_kernel("binary_vec_kernel", binary_vec_kernel<T, OP>, dim3(grid),
+                                                dim3(kThreads), 0, stream, nullptr, static_cast<T*>(out),
+                                                static_cast<const T*>(a), static_cast<const T*>(b), n)) {
+      return launch_status;
+    }
   } else {
     const int64_t need = (n + kThreads - 1) / kThreads;
     const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min(need, cap)));
-    binary_scalar_kernel<T, OP><<<grid, kThreads, 0, stream>>>(static_cast<T*>(out), static_cast<const T*>(a),
-                                                              static_cast<const T*>(b), n);
+    if (const int launch_status = launch_kernel("binary_scalar_kernel", binary_scalar_kernel<T, OP>, dim3(grid),
+                                                dim3(kThreads), 0, stream, nullptr, static_cast<T*>(out),
+                                                static_cast<const T*>(a), static_cast<const T*>(b), n)) {
+      return launch_status;
+    }
   }
   return check_launch(what);
 }

@@ -36,6 +36,7 @@ struct GatherArgs {
 // Vector path: bytes of a row are copied as 16-byte words (the row pitch and
 // both base pointers are 16-byte multiples).
 __global__ void __launch_bounds__(kThreads) gather_vec_kernel(GatherArgs a) {
+  grid_dependency_wait();
   const int G = a.group;
   const int rows_per_block = kThreads / G;
   const int gi = threadIdx.x / G;
@@ -69,6 +70,7 @@ __global__ void __launch_bounds__(kThreads) gather_vec_kernel(GatherArgs a) {
 // Scalar path: element-wise copy of the raw storage (no conversion).
 template <typename W>
 __global__ void __launch_bounds__(kThreads) gather_scalar_kernel(GatherArgs a) {
+  grid_dependency_wait();
   for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
     const int32_t id = a.ids[row];
     if (id < 0 || id >= a.vocab) {
@@ -117,13 +119,22 @@ extern "C" int bm_embed_gather(void* out, const void* table, const int32_t* ids,
     const int rows_per_block = kThreads / g;
     const int64_t need = (rows + rows_per_block - 1) / rows_per_block;
     const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min(need, cap)));
-    gather_vec_kernel<<<grid, kThreads, 0, s>>>(a);
+    if (const int launch_status = launch_kernel("gather_vec_kernel", gather_vec_kernel, dim3(grid), dim3(kThreads), 0,
+                                                s, nullptr, a)) {
+      return launch_status;
+    }
   } else {
     const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min(rows, cap)));
     if (es == 4) {
-      gather_scalar_kernel<uint32_t><<<grid, kThreads, 0, s>>>(a);
+      if (const int launch_status = launch_kernel("gather_scalar_kernel", gather_scalar_kernel<uint32_t>, dim3(grid),
+                                                  dim3(kThreads), 0, s, nullptr, a)) {
+        return launch_status;
+      }
     } else {
-      gather_scalar_kernel<uint16_t><<<grid, kThreads, 0, s>>>(a);
+      if (const int launch_status = launch_kernel("gather_scalar_kernel", gather_scalar_kernel<uint16_t>, dim3(grid),
+                                                  dim3(kThreads), 0, s, nullptr, a)) {
+        return launch_status;
+      }
     }
   }
   return check_launch("bm_embed_gather");

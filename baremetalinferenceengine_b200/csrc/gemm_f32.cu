@@ -75,6 +75,7 @@ __device__ __forceinline__ void load_b_row(const float* b, int n, int k, int c0,
 // models): loads issued a round at a time, at more registers per thread.
 template <int MT, bool VEC, bool SWIGLU, bool SHORT>
 __global__ void __launch_bounds__(kThreads) gemm_f32_kernel(const Args p) {
+  grid_dependency_wait();
   constexpr int kAcc = SWIGLU ? 2 : 1;
   __shared__ __align__(16) float red[kAcc][kWarps][MT][kCols];
   cg::cluster_group cluster = cg::this_cluster();
@@ -192,29 +193,22 @@ __global__ void __launch_bounds__(kThreads) gemm_f32_kernel(const Args p) {
 template <int MT, bool SWIGLU>
 int launch_mt(const Args& p, int col_blocks, int row_tiles, int ks, bool vec, cudaStream_t stream,
               const char* what) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(col_blocks * ks), static_cast<unsigned>(row_tiles), 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(ks);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const bool short_k = p.k_per_cta <= kShortK;
-  cudaError_t err;
-  if (short_k) {
-    err = vec ? cudaLaunchKernelEx(&cfg, gemm_f32_kernel<MT, true, SWIGLU, true>, p)
-              : cudaLaunchKernelEx(&cfg, gemm_f32_kernel<MT, false, SWIGLU, true>, p);
-  } else {
-    err = vec ? cudaLaunchKernelEx(&cfg, gemm_f32_kernel<MT, true, SWIGLU, false>, p)
-              : cudaLaunchKernelEx(&cfg, gemm_f32_kernel<MT, false, SWIGLU, false>, p);
+  const dim3 grid(static_cast<unsigned>(col_blocks * ks), static_cast<unsigned>(row_tiles), 1);
+  cudaLaunchAttribute cluster;
+  cluster.id = cudaLaunchAttributeClusterDimension;
+  cluster.val.clusterDim.x = static_cast<unsigned>(ks);
+  cluster.val.clusterDim.y = 1;
+  cluster.val.clusterDim.z = 1;
+  if (p.k_per_cta <= kShortK) {
+    return vec ? launch_kernel(what, gemm_f32_kernel<MT, true, SWIGLU, true>, grid, dim3(kThreads), 0, stream,
+                               &cluster, p)
+               : launch_kernel(what, gemm_f32_kernel<MT, false, SWIGLU, true>, grid, dim3(kThreads), 0, stream,
+                               &cluster, p);
   }
-  if (err != cudaSuccess) return fail(BM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
-  return check_launch(what);
+  return vec ? launch_kernel(what, gemm_f32_kernel<MT, true, SWIGLU, false>, grid, dim3(kThreads), 0, stream,
+                             &cluster, p)
+             : launch_kernel(what, gemm_f32_kernel<MT, false, SWIGLU, false>, grid, dim3(kThreads), 0, stream,
+                             &cluster, p);
 }
 
 // Plans and launches: the rows in tiles of MT (at most max_mt), the column blocks

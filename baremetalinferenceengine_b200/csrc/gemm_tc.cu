@@ -89,6 +89,7 @@ template <bool SWIGLU>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb0,
                    const __grid_constant__ CUtensorMap tb1, const Args a) {
+  grid_dependency_wait();
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // stages 1024-byte aligned (the swizzle atom); barriers after them
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -315,6 +316,7 @@ template <bool SWIGLU>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb0,
                         const __grid_constant__ CUtensorMap tb1, const Args a) {
+  grid_dependency_wait();
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                          ~static_cast<uintptr_t>(1023));
@@ -546,13 +548,19 @@ int run(const char* what, void* out, const void* x, const void* w0, const void* 
     const int grid = 2 * static_cast<int>(std::min<int64_t>(tiles, sm_count() / 2));
     auto kernel = gemm_tc_pair_kernel<SWIGLU>;
     if (int st = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), kPairSmemBytes, what)) return st;
-    kernel<<<grid, kThreads, kPairSmemBytes, as_stream(stream)>>>(ta, tb0, tb1, a);
+    if (const int launch_status = launch_kernel(what, kernel, dim3(grid), dim3(kThreads), kPairSmemBytes,
+                                                as_stream(stream), nullptr, ta, tb0, tb1, a)) {
+      return launch_status;
+    }
     return check_launch(what);
   }
   const int grid = static_cast<int>(std::min<int64_t>(tiles, sm_count()));
   auto kernel = gemm_tc_kernel<SWIGLU>;
   if (int st = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), kSmemBytes, what)) return st;
-  kernel<<<grid, kThreads, kSmemBytes, as_stream(stream)>>>(ta, tb0, tb1, a);
+  if (const int launch_status = launch_kernel(what, kernel, dim3(grid), dim3(kThreads), kSmemBytes,
+                                              as_stream(stream), nullptr, ta, tb0, tb1, a)) {
+    return launch_status;
+  }
   return check_launch(what);
 }
 

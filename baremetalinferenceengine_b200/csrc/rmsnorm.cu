@@ -42,6 +42,7 @@ struct RmsArgs {
 
 template <typename T, int VPT, bool FUSED, int MAXT>
 __global__ void __launch_bounds__(MAXT) rmsnorm_vec_kernel(RmsArgs a) {
+  grid_dependency_wait();
   constexpr int N = VecWidth<T>::value;
   __shared__ float s_part[2][kMaxWarpsPerGroup];  // [parity][warp of block]
 
@@ -135,6 +136,7 @@ __global__ void __launch_bounds__(MAXT) rmsnorm_vec_kernel(RmsArgs a) {
 // One 256-thread block per row; two passes over the row (sum, then write).
 template <typename T, bool FUSED>
 __global__ void __launch_bounds__(256) rmsnorm_scalar_kernel(RmsArgs a) {
+  grid_dependency_wait();
   __shared__ float s_warp[8];
   for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
     T* in_row = static_cast<T*>(a.residual) + row * a.in_stride;
@@ -173,19 +175,34 @@ int launch_vec(RmsArgs a, int vpt, cudaStream_t stream) {
   const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min(need, cap)));
   switch (vpt) {
     case 1:
-      rmsnorm_vec_kernel<T, 1, FUSED, 256><<<grid, block, 0, stream>>>(a);
+      if (const int launch_status = launch_kernel("rmsnorm_vec_kernel", rmsnorm_vec_kernel<T, 1, FUSED, 256>,
+                                                  dim3(grid), dim3(block), 0, stream, nullptr, a)) {
+        return launch_status;
+      }
       break;
     case 2:
-      rmsnorm_vec_kernel<T, 2, FUSED, 256><<<grid, block, 0, stream>>>(a);
+      if (const int launch_status = launch_kernel("rmsnorm_vec_kernel", rmsnorm_vec_kernel<T, 2, FUSED, 256>,
+                                                  dim3(grid), dim3(block), 0, stream, nullptr, a)) {
+        return launch_status;
+      }
       break;
     case 4:
-      rmsnorm_vec_kernel<T, 4, FUSED, 256><<<grid, block, 0, stream>>>(a);
+      if (const int launch_status = launch_kernel("rmsnorm_vec_kernel", rmsnorm_vec_kernel<T, 4, FUSED, 256>,
+                                                  dim3(grid), dim3(block), 0, stream, nullptr, a)) {
+        return launch_status;
+      }
       break;
     default:
       if (block <= 256) {
-        rmsnorm_vec_kernel<T, 8, FUSED, 256><<<grid, block, 0, stream>>>(a);
+        if (const int launch_status = launch_kernel("rmsnorm_vec_kernel", rmsnorm_vec_kernel<T, 8, FUSED, 256>,
+                                                    dim3(grid), dim3(block), 0, stream, nullptr, a)) {
+          return launch_status;
+        }
       } else {
-        rmsnorm_vec_kernel<T, 8, FUSED, 1024><<<grid, block, 0, stream>>>(a);
+        if (const int launch_status = launch_kernel("rmsnorm_vec_kernel", rmsnorm_vec_kernel<T, 8, FUSED, 1024>,
+                                                    dim3(grid), dim3(block), 0, stream, nullptr, a)) {
+          return launch_status;
+        }
       }
       break;
   }
@@ -196,7 +213,10 @@ template <typename T, bool FUSED>
 int launch_scalar(RmsArgs a, cudaStream_t stream) {
   const int64_t cap = static_cast<int64_t>(sm_count()) * 8 * 64;
   const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min(a.rows, cap)));
-  rmsnorm_scalar_kernel<T, FUSED><<<grid, 256, 0, stream>>>(a);
+  if (const int launch_status = launch_kernel("rmsnorm_scalar_kernel", rmsnorm_scalar_kernel<T, FUSED>, dim3(grid),
+                                              dim3(256), 0, stream, nullptr, a)) {
+    return launch_status;
+  }
   return check_launch(FUSED ? "bm_add_rmsnorm" : "bm_rmsnorm");
 }
 

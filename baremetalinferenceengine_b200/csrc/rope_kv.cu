@@ -167,6 +167,7 @@ __device__ __forceinline__ void finish_unit(const RopeArgs& a, const Unit& u, in
 
 template <typename T, int VEC, int MODE>
 __global__ void __launch_bounds__(256) rope_kv_kernel(RopeArgs a) {
+  grid_dependency_wait();
   __shared__ float2 cs[kMaxHalf];
   const int tid = threadIdx.x;
   const int nthreads = blockDim.x;
@@ -263,6 +264,7 @@ __device__ __forceinline__ void rotate(Chunk<T, VEC>& c1, Chunk<T, VEC>& c2, con
 
 template <typename T, int VEC, int MODE>
 __global__ void __launch_bounds__(256, BM_ROPE_WARP_MINB) rope_kv_warp_kernel(RopeArgs a) {
+  grid_dependency_wait();
   constexpr int U = kWarpUnroll;
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -384,6 +386,7 @@ __global__ void __launch_bounds__(256, BM_ROPE_WARP_MINB) rope_kv_warp_kernel(Ro
 }
 
 __global__ void rope_table_kernel(float2* table, int32_t max_pos, int half, int hd, double theta) {
+  grid_dependency_wait();
   const int64_t n = static_cast<int64_t>(max_pos) * half;
   for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < n;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -401,14 +404,20 @@ int launch_typed(const RopeArgs& a, cudaStream_t stream, const char* what) {
   if (a.rows >= kWarpKernelMinRows && (MODE == kStore || (a.upv >= 1 && a.upv <= 32))) {
     const int64_t blocks = (a.rows + 7) / 8;  // 8 warps (tokens in flight) per 256-thread block
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(blocks, static_cast<int64_t>(sm_count()) * 16));
-    rope_kv_warp_kernel<T, VEC, MODE><<<grid, 256, 0, stream>>>(a);
+    if (const int launch_status = launch_kernel("rope_kv_warp_kernel", rope_kv_warp_kernel<T, VEC, MODE>, dim3(grid),
+                                                dim3(256), 0, stream, nullptr, a)) {
+      return launch_status;
+    }
     return check_launch(what);
   }
   const int want = (a.total_units + kUPT - 1) / kUPT;
   const int block = std::min(256, std::max(64, (want + 31) / 32 * 32));
   const int64_t cap = static_cast<int64_t>(sm_count()) * (2048 / block);
   const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min(a.rows, cap)));
-  rope_kv_kernel<T, VEC, MODE><<<grid, block, 0, stream>>>(a);
+  if (const int launch_status = launch_kernel("rope_kv_kernel", rope_kv_kernel<T, VEC, MODE>, dim3(grid), dim3(block),
+                                              0, stream, nullptr, a)) {
+    return launch_status;
+  }
   return check_launch(what);
 }
 
@@ -578,7 +587,11 @@ extern "C" int bm_rope_table_fill(void* table, int32_t max_pos, int32_t head_dim
   const int half = head_dim / 2;
   const int64_t n = static_cast<int64_t>(max_pos) * half;
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, static_cast<int64_t>(sm_count()) * 8));
-  rope_table_kernel<<<grid, 256, 0, as_stream(stream)>>>(static_cast<float2*>(table), max_pos, half, head_dim, theta);
+  if (const int launch_status = launch_kernel("rope_table_kernel", rope_table_kernel, dim3(grid), dim3(256), 0,
+                                              as_stream(stream), nullptr, static_cast<float2*>(table), max_pos, half,
+                                              head_dim, theta)) {
+    return launch_status;
+  }
   return check_launch(what);
 }
 

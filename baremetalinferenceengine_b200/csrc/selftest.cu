@@ -16,6 +16,7 @@ namespace {
 // result[1] / [3]: their durations in ns.
 __global__ void __launch_bounds__(64) bounded_wait_selftest_kernel(int32_t* status, uint64_t limit_ns,
                                                                    int64_t* result) {
+  grid_dependency_wait();
   __shared__ __align__(8) uint64_t bar;
   __shared__ int abort_flag;
   if (threadIdx.x == 0) {
@@ -49,6 +50,10 @@ extern "C" int bm_selftest_bounded_wait(int64_t limit_ns, int32_t* d_status, int
   if (limit_ns < 1000000 || limit_ns > 2000000000) {
     return fail(BM_ERR_INVALID_ARGUMENT, "%s: limit_ns outside [1 ms, 2 s]", what);
   }
-  bounded_wait_selftest_kernel<<<1, 64, 0, as_stream(stream)>>>(d_status, static_cast<uint64_t>(limit_ns), d_result);
+  if (const int launch_status = launch_kernel("bounded_wait_selftest_kernel", bounded_wait_selftest_kernel, dim3(1),
+                                              dim3(64), 0, as_stream(stream), nullptr, d_status,
+                                              static_cast<uint64_t>(limit_ns), d_result)) {
+    return launch_status;
+  }
   return check_launch(what);
 }

@@ -21,6 +21,7 @@ __device__ __forceinline__ void merge(float& m, float& s, float m2, float s2) {
 
 template <typename T>
 __global__ void __launch_bounds__(kSoftmaxThreads) softmax_kernel(T* x, int64_t size, int64_t stride) {
+  grid_dependency_wait();
   __shared__ float sm[kSoftmaxThreads / 32], ss[kSoftmaxThreads / 32];
   T* v = x + static_cast<int64_t>(blockIdx.x) * stride;
   float m = -INFINITY, s = 0.f;
@@ -67,9 +68,17 @@ extern "C" int bm_softmax(void* x, int64_t size, int64_t num_vectors, int64_t st
   if (!x) return fail(BM_ERR_INVALID_ARGUMENT, "bm_softmax: NULL x");
   const dim3 grid(static_cast<unsigned>(num_vectors));
   if (dtype == BM_F32) {
-    softmax_kernel<float><<<grid, kSoftmaxThreads, 0, as_stream(stream)>>>(static_cast<float*>(x), size, stride);
+    if (const int launch_status = launch_kernel("softmax_kernel", softmax_kernel<float>, dim3(grid),
+                                                dim3(kSoftmaxThreads), 0, as_stream(stream), nullptr,
+                                                static_cast<float*>(x), size, stride)) {
+      return launch_status;
+    }
   } else {
-    softmax_kernel<bf16><<<grid, kSoftmaxThreads, 0, as_stream(stream)>>>(static_cast<bf16*>(x), size, stride);
+    if (const int launch_status = launch_kernel("softmax_kernel", softmax_kernel<bf16>, dim3(grid),
+                                                dim3(kSoftmaxThreads), 0, as_stream(stream), nullptr,
+                                                static_cast<bf16*>(x), size, stride)) {
+      return launch_status;
+    }
   }
   return check_launch("bm_softmax");
 }
