@@ -33,6 +33,7 @@ ExecutionEngine::ExecutionEngine(std::shared_ptr<MemoryAllocator> allocator, std
   }
   const int max_seq = kv_cache_->get_max_seq_len();
   logits_ = std::make_shared<DeviceBuffer<float>>(config_.vocab_size);
+  CUDA_CHECK(cudaMallocHost(&logits_host_, sizeof(float) * config_.vocab_size));
   // (cos, sin) per position, computed once on the device in fp64 and kept in L2-sized fp32
   rope_table_ = std::make_shared<DeviceBuffer<float>>(static_cast<size_t>(max_seq) * config_.head_dim());
   CUDA_CHECK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
@@ -44,6 +45,7 @@ ExecutionEngine::ExecutionEngine(std::shared_ptr<MemoryAllocator> allocator, std
 ExecutionEngine::~ExecutionEngine() {
   if (decode_graph_) cudaGraphExecDestroy(decode_graph_);
   if (staging_) cudaFreeHost(staging_);
+  if (logits_host_) cudaFreeHost(logits_host_);
   if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -71,9 +73,7 @@ void ExecutionEngine::reserve(int tokens) {
   attention_out_ = buffer(n * dim);
   projected_ = buffer(n * dim);
   activated_ = buffer(n * hidden);
-  ids_ = std::make_shared<DeviceBuffer<int>>(n);
-  positions_ = std::make_shared<DeviceBuffer<int>>(n);
-  lens_ = std::make_shared<DeviceBuffer<int>>(n);
+  token_args_ = std::make_shared<DeviceBuffer<int>>(3 * n);
   if (staging_) CUDA_CHECK(cudaFreeHost(staging_));
   CUDA_CHECK(cudaMallocHost(&staging_, 3 * n * sizeof(int)));
   size_t ws = 0;
@@ -104,17 +104,18 @@ std::vector<float> ExecutionEngine::forward(const std::vector<int>& input_tokens
   const int T = static_cast<int>(input_tokens.size());
   reserve(T);
   const int pos0 = kv_cache_->get_current_seq_pos();
-  // ids, positions and attended lengths (token t: pos0 + t + 1) via pinned staging
+  // ids, positions and attended lengths (token t: pos0 + t + 1), laid out
+  // [ids | positions | lengths] in pinned staging and sent in one copy; for one
+  // token the device pointers are always the same, as the decode graph needs
   for (int t = 0; t < T; ++t) {
     staging_[t] = input_tokens[t];
-    staging_[capacity_ + t] = pos0 + t;
-    staging_[2 * capacity_ + t] = pos0 + t + 1;
+    staging_[T + t] = pos0 + t;
+    staging_[2 * T + t] = pos0 + t + 1;
   }
-  CUDA_CHECK(cudaMemcpyAsync(ids_->get(), staging_, sizeof(int) * T, cudaMemcpyHostToDevice, stream_));
-  CUDA_CHECK(cudaMemcpyAsync(positions_->get(), staging_ + capacity_, sizeof(int) * T, cudaMemcpyHostToDevice,
-                             stream_));
-  CUDA_CHECK(cudaMemcpyAsync(lens_->get(), staging_ + 2 * capacity_, sizeof(int) * T, cudaMemcpyHostToDevice,
-                             stream_));
+  ids_ = token_args_->get();
+  positions_ = ids_ + T;
+  lens_ = ids_ + 2 * T;
+  CUDA_CHECK(cudaMemcpyAsync(ids_, staging_, sizeof(int) * 3 * T, cudaMemcpyHostToDevice, stream_));
 
   if (T > 1) {
     run(T, pos0 + T);
@@ -148,11 +149,12 @@ std::vector<float> ExecutionEngine::forward(const std::vector<int>& input_tokens
   }
   kv_cache_->increment_seq_pos(T);
 
-  std::vector<float> logits(config_.vocab_size);
-  CUDA_CHECK(cudaMemcpyAsync(logits.data(), logits_->get(), logits.size() * sizeof(float), cudaMemcpyDeviceToHost,
-                             stream_));
+  // the logits come back through pinned memory (a pageable destination would be
+  // staged by the driver)
+  CUDA_CHECK(cudaMemcpyAsync(logits_host_, logits_->get(), sizeof(float) * config_.vocab_size,
+                             cudaMemcpyDeviceToHost, stream_));
   CUDA_CHECK(cudaStreamSynchronize(stream_));
-  return logits;
+  return std::vector<float>(logits_host_, logits_host_ + config_.vocab_size);
 }
 
 void ExecutionEngine::run(int T, int max_len) {
@@ -162,7 +164,7 @@ void ExecutionEngine::run(int T, int max_len) {
   const int head_dim = config_.head_dim();
   const int max_seq = kv_cache_->get_max_seq_len();
   const float eps = config_.norm_eps;
-  check(bm_embed_gather(hidden_, token_embeddings_, ids_->get(), T, dim, config_.vocab_size, dim, BM_F32, nullptr,
+  check(bm_embed_gather(hidden_, token_embeddings_, ids_, T, dim, config_.vocab_size, dim, BM_F32, nullptr,
                         stream_),
         "bm_embed_gather");
 
@@ -187,12 +189,12 @@ void ExecutionEngine::run(int T, int max_len) {
             "bm_gemm_shared_a");
     }
     // Token t at cache position positions_[t] of the one sequence the reference's cache holds.
-    check(bm_rope_kv_store(q_, k_, v_, positions_->get(), 0, nullptr, k_cache, v_cache, rope_table_->get(),
+    check(bm_rope_kv_store(q_, k_, v_, positions_, 0, nullptr, k_cache, v_cache, rope_table_->get(),
                            max_seq, config_.rope_theta, T, heads, heads, head_dim, max_seq, 1, BM_F32, nullptr,
                            stream_),
           "bm_rope_kv_store");
     // All T tokens' attention in one launch: query t over cache positions [0, lens_[t]).
-    check(bm_decode_attention(attention_out_, q_, k_cache, v_cache, nullptr, lens_->get(), max_len, T, heads,
+    check(bm_decode_attention(attention_out_, q_, k_cache, v_cache, nullptr, lens_, max_len, T, heads,
                               heads, head_dim, max_seq, 1, 0.f, attention_workspace_->get(),
                               attention_workspace_->size(), BM_F32, nullptr, stream_),
           "bm_decode_attention");

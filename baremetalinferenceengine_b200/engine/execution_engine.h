@@ -88,7 +88,8 @@ class ExecutionEngine {
   float* attention_out_ = nullptr;
   float* projected_ = nullptr;
   float* activated_ = nullptr;
-  std::shared_ptr<DeviceBuffer<int>> ids_;
+  std::shared_ptr<DeviceBuffer<int>> token_args_;  // [3][capacity]: a call's ids, positions, lens
+  int* ids_ = nullptr;                             // this call's three arrays in token_args_
   // Every layer and the logits of the last token for T tokens on stream_;
   // attention planned for at most max_len attended positions.
   void run(int T, int max_len);
@@ -98,8 +99,9 @@ class ExecutionEngine {
   int graph_capacity_ = -1;                 // capacity_ when the graph was captured
   int eager_decode_steps_ = 0;              // one-token forwards run before the capture
   int* staging_ = nullptr;                  // pinned host: ids, positions, lens of a call
-  std::shared_ptr<DeviceBuffer<int>> positions_;           // cache position per token
-  std::shared_ptr<DeviceBuffer<int>> lens_;                // attended positions per token
+  int* positions_ = nullptr;                // cache position per token
+  int* lens_ = nullptr;                     // attended positions per token
+  float* logits_host_ = nullptr;            // pinned host: the last token's logits
   std::shared_ptr<DeviceBuffer<char>> attention_workspace_;  // split partials of decode attention
 
   std::shared_ptr<DeviceBuffer<float>> logits_;  // [vocab]
