@@ -829,8 +829,11 @@ def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
     # (throughput in GB/s does not depend on R once R is thousands of tokens).
     R = int(min(shape.rows, 0.4 * avail / world // io_per_row))
     R = int(-max_over_ranks([-R])[0])  # the same rows (and the same branch) on every rank
-    if R < 1024:
+    if R < min(shape.rows, 1024):
         return {"unavailable": f"host has {avail / 1e9:.1f} GB free: too little to pin a step's buffers"}
+    # A step that fits in L2 is a decode-sized batch: one copy in, one launch
+    # sequence, one copy out, repeated enough times to time.
+    small = shape.step_bytes() < L2_RESIDENT_BYTES
 
     def pinned(t):
         return torch.empty((R,) + tuple(t.shape[1:]), dtype=t.dtype, device="cpu", pin_memory=True)
@@ -840,7 +843,7 @@ def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
     for n in names_in:
         h_in[n].copy_(getattr(b, n)[:R])
     h2d, comp, d2h = (torch.cuda.Stream(dev) for _ in range(3))
-    chunks = max(1, min(args.e2e_chunks, R))
+    chunks = 1 if small else max(1, min(args.e2e_chunks, R))
     size = math.ceil(R / chunks)
     slices = [slice(i, min(R, i + size)) for i in range(0, R, size)]
     done = torch.cuda.Event()
@@ -867,7 +870,7 @@ def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
     for _ in range(2):
         step()
     torch.cuda.synchronize(dev)
-    E = max(1, args.e2e_steps)
+    E = max(50 if small else 1, args.e2e_steps)
     barrier()
     torch.cuda.synchronize(dev)
     t0 = torch.cuda.Event(enable_timing=True)
@@ -886,7 +889,7 @@ def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
     h2d_rate = bytes_per_row(b, names_in) * R / (ms / E / 1e3) / 1e9
     return {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": int(bytes_per_row(b, names_in) * R),
             "d2h_bytes_per_step": int(bytes_per_row(b, names_out) * R), "rows_per_step": R, "steps": E,
-            "ms_per_step": round(ms / E, 2), "chunks": len(slices),
+            "ms_per_step": round(ms / E, 4), "chunks": len(slices),
             "link": link, "h2d_gbs_achieved": round(h2d_rate, 1),
             "frac_of_link": round(h2d_rate / link["h2d_gbs"], 3) if link.get("h2d_gbs") else None,
             "how": "per step: pinned-host -> device copies of every input, the five kernels, device -> pinned-host "
