@@ -455,7 +455,10 @@ int launch_tc(const AttnArgs& a, cudaStream_t stream);
 // pairs (fewer pairs are split evenly by the per-pair grid already, which starts
 // faster); workspace: balanced_workspace_bytes(group, ctas).
 constexpr int kBalancedMaxBatch = 2048;
-constexpr int kBalancedMinPairs = 32;
+#ifndef BM_ATTN_BALANCED_MIN_PAIRS
+#define BM_ATTN_BALANCED_MIN_PAIRS 32
+#endif
+constexpr int kBalancedMinPairs = BM_ATTN_BALANCED_MIN_PAIRS;
 bool balanced_eligible(const AttnArgs& a, bm_dtype_t dtype);
 size_t balanced_workspace_bytes(int group, int ctas);
 int launch_tc_balanced(AttnArgs a, int ctas, cudaStream_t stream);

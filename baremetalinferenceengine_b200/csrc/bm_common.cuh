@@ -133,6 +133,43 @@ __device__ __forceinline__ void raise_status(int32_t* status, int32_t bits) {
 // launch (launch_kernel), a kernel may start while the one before it on the stream
 // is finishing; this waits until that kernel has completed and its writes are
 // visible, before any read or write of memory. A no-op for a normal launch.
-__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// It then lets the next kernel on the stream launch (launch_dependents): that
+// kernel's blocks may become resident while this one runs, and they wait in
+// their own grid_dependency_wait until this whole grid has completed and its
+// writes are visible, so an early trigger changes when blocks are placed, never
+// what they read. BM_PDL_TRIGGER=0 at build time leaves the trigger to grid exit.
+#ifndef BM_PDL_TRIGGER
+#define BM_PDL_TRIGGER 1
+#endif
+#ifndef BM_PDL_PREFETCH
+#define BM_PDL_PREFETCH 1
+#endif
+
+// Asks L2 for the 128-byte line holding p and does not wait for it. Kernels
+// issue it for their first addresses before grid_dependency_wait, so the DRAM
+// latency of their first loads overlaps the previous kernel instead of following
+// it. It cannot change what a later load returns: L2 is where every SM's writes
+// land, so a line fetched early and then written by the previous kernel holds
+// the written bytes when this kernel reads it after the wait.
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+#if BM_PDL_PREFETCH
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+#else
+  (void)p;
+#endif
+}
+// prefetch_l2 over [p, p + bytes), one line per participant per step.
+__device__ __forceinline__ void prefetch_l2_range(const void* p, int64_t bytes, int idx, int count) {
+  const char* c = static_cast<const char*>(p);
+  for (int64_t off = static_cast<int64_t>(idx) * 128; off < bytes; off += static_cast<int64_t>(count) * 128) {
+    prefetch_l2(c + off);
+  }
+}
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+#if BM_PDL_TRIGGER
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+#endif
+}
 
 }  // namespace bm

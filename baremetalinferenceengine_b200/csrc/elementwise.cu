@@ -60,9 +60,17 @@ __device__ __forceinline__ float apply(float a, float b) {
 template <typename T, Op OP>
 __global__ void __launch_bounds__(kThreads, BM_EW_MINB) binary_vec_kernel(T* out, const T* a, const T* b,
                                                              int64_t n) {
-  grid_dependency_wait();
   constexpr int N = VecWidth<T>::value;
   const int64_t nvec = n / N;
+#pragma unroll
+  for (int j = 0; j < kUnroll; ++j) {  // the first trip's lines, while the previous kernel finishes
+    const int64_t v = static_cast<int64_t>(blockIdx.x) * kThreads * kUnroll + threadIdx.x + j * kThreads;
+    if (v < nvec) {
+      prefetch_l2(a + v * N);
+      prefetch_l2(b + v * N);
+    }
+  }
+  grid_dependency_wait();
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * kThreads * kUnroll + threadIdx.x; base < nvec;
        base += stride * kUnroll) {

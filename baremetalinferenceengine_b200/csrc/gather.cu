@@ -36,11 +36,15 @@ struct GatherArgs {
 // Vector path: bytes of a row are copied as 16-byte words (the row pitch and
 // both base pointers are 16-byte multiples).
 __global__ void __launch_bounds__(kThreads) gather_vec_kernel(GatherArgs a) {
-  grid_dependency_wait();
   const int G = a.group;
   const int rows_per_block = kThreads / G;
   const int gi = threadIdx.x / G;
   const int t = threadIdx.x - gi * G;
+  {  // the first row's id (the table row it names is known only after the wait)
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * rows_per_block + gi;
+    if (t == 0 && row < a.rows) prefetch_l2(a.ids + row);
+  }
+  grid_dependency_wait();
   const int64_t row_bytes = a.nv * 16;
   for (int64_t row = static_cast<int64_t>(blockIdx.x) * rows_per_block + gi; row < a.rows;
        row += static_cast<int64_t>(gridDim.x) * rows_per_block) {

@@ -42,7 +42,6 @@ struct RmsArgs {
 
 template <typename T, int VPT, bool FUSED, int MAXT>
 __global__ void __launch_bounds__(MAXT) rmsnorm_vec_kernel(RmsArgs a) {
-  grid_dependency_wait();
   constexpr int N = VecWidth<T>::value;
   __shared__ float s_part[2][kMaxWarpsPerGroup];  // [parity][warp of block]
 
@@ -54,6 +53,16 @@ __global__ void __launch_bounds__(MAXT) rmsnorm_vec_kernel(RmsArgs a) {
   const int warps_per_group = G >> 5;
   const int first_warp = gi * warps_per_group;
   const T* weight = static_cast<const T*>(a.weight);
+  {  // the first row's lines, while the previous kernel finishes
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * rows_per_block + gi;
+    if (row < a.rows) {
+      const int64_t bytes = static_cast<int64_t>(a.nv) * 16;
+      prefetch_l2_range(static_cast<const T*>(a.residual) + row * a.in_stride, bytes, t, G);
+      if constexpr (FUSED) prefetch_l2_range(static_cast<const T*>(a.delta) + row * a.in_stride, bytes, t, G);
+      if (gi == 0) prefetch_l2_range(weight, bytes, t, G);
+    }
+  }
+  grid_dependency_wait();
 
   int parity = 0;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * rows_per_block; base < a.rows;

@@ -165,8 +165,28 @@ __device__ __forceinline__ void finish_unit(const RopeArgs& a, const Unit& u, in
   c2.store(dst + a.half);
 }
 
+// prefetch_l2 of one token's position, sequence id and q / k / v rows: the lines
+// its first loads will touch (idx of count participants).
+template <typename T, int MODE>
+__device__ __forceinline__ void prefetch_token(const RopeArgs& a, int64_t row, int idx, int count) {
+  if (row >= a.rows) return;
+  if (idx == 0) {
+    if (a.positions) prefetch_l2(a.positions + row);
+    if (a.seq_ids) prefetch_l2(a.seq_ids + row);
+  }
+  const int64_t es = sizeof(T);
+  if (MODE != kStore) {
+    prefetch_l2_range(static_cast<const T*>(a.q) + row * a.hq * a.hd, a.hq * a.hd * es, idx, count);
+    prefetch_l2_range(static_cast<const T*>(a.k) + row * a.hkv * a.hd, a.hkv * a.hd * es, idx, count);
+  }
+  if (MODE != kRope) {
+    prefetch_l2_range(static_cast<const T*>(a.v) + row * a.hkv * a.hd, a.hkv * a.hd * es, idx, count);
+  }
+}
+
 template <typename T, int VEC, int MODE>
 __global__ void __launch_bounds__(256) rope_kv_kernel(RopeArgs a) {
+  prefetch_token<T, MODE>(a, blockIdx.x, threadIdx.x, blockDim.x);
   grid_dependency_wait();
   __shared__ float2 cs[kMaxHalf];
   const int tid = threadIdx.x;
@@ -174,6 +194,14 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(RopeArgs a) {
   const int64_t cache_head_stride = static_cast<int64_t>(a.max_seq) * a.hd;
 
   for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    // This thread's first UPT units' loads go out with the position's, before the
+    // table barrier (a row found bad below discards them).
+    Chunk<T, VEC> c1[kUPT], c2[kUPT];
+#pragma unroll
+    for (int j = 0; j < kUPT; ++j) {
+      const int u = tid + j * nthreads;
+      if (u < a.total_units) load_unit<T, VEC, MODE>(a, decode(a, u), row, c1[j], c2[j]);
+    }
     const int32_t pos = a.positions ? a.positions[row] : static_cast<int32_t>(a.pos0 + row);
     const int32_t seq = a.seq_ids ? a.seq_ids[row] : 0;
     int32_t bad = 0;
@@ -189,14 +217,6 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(RopeArgs a) {
     }
     const int64_t cache_base =
         MODE == kRope ? 0 : (static_cast<int64_t>(seq) * a.hkv * a.max_seq + pos) * a.hd;
-
-    // Issue this thread's first UPT units' loads before the table barrier.
-    Chunk<T, VEC> c1[kUPT], c2[kUPT];
-#pragma unroll
-    for (int j = 0; j < kUPT; ++j) {
-      const int u = tid + j * nthreads;
-      if (u < a.total_units) load_unit<T, VEC, MODE>(a, decode(a, u), row, c1[j], c2[j]);
-    }
 
     if (MODE != kStore) {
       for (int i = tid; i < a.half; i += nthreads) {
@@ -262,12 +282,15 @@ __device__ __forceinline__ void rotate(Chunk<T, VEC>& c1, Chunk<T, VEC>& c2, con
   c2.set(x2);
 }
 
-template <typename T, int VEC, int MODE>
+// TABLE: (cos, sin) from the table (a.table != NULL); otherwise computed in fp64,
+// whose pow / sincos need far more registers, so each form gets its own build.
+template <typename T, int VEC, int MODE, bool TABLE>
 __global__ void __launch_bounds__(256, BM_ROPE_WARP_MINB) rope_kv_warp_kernel(RopeArgs a) {
-  grid_dependency_wait();
   constexpr int U = kWarpUnroll;
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  prefetch_token<T, MODE>(a, warp, lane, 32);
+  grid_dependency_wait();
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   const int upv = MODE == kStore ? 1 : a.upv;  // host guarantees 1 <= upv <= 32 for pair modes
   const int hpi = 32 / upv;
@@ -286,7 +309,7 @@ __global__ void __launch_bounds__(256, BM_ROPE_WARP_MINB) rope_kv_warp_kernel(Ro
       if (pos >= a.max_seq) bad |= BM_DEVERR_BAD_POSITION;
       if (seq < 0 || seq >= a.num_seqs) bad |= BM_DEVERR_BAD_SEQUENCE;
     }
-    if (MODE != kStore && a.table != nullptr && pos >= a.table_len) bad |= BM_DEVERR_BAD_POSITION;
+    if (MODE != kStore && TABLE && pos >= a.table_len) bad |= BM_DEVERR_BAD_POSITION;
     if (bad) {  // uniform across the warp
       if (lane == 0) raise_status(a.status, bad);
       continue;
@@ -294,9 +317,9 @@ __global__ void __launch_bounds__(256, BM_ROPE_WARP_MINB) rope_kv_warp_kernel(Ro
     const int64_t cache_base =
         MODE == kRope ? 0 : (static_cast<int64_t>(seq) * a.hkv * a.max_seq + pos) * a.hd;
 
+    float2 cs[VEC];
     if (pair_lane) {
-      float2 cs[VEC];
-      if (a.table != nullptr) {
+      if constexpr (TABLE) {
         const float2* t = a.table + static_cast<int64_t>(pos) * a.half + c * VEC;
         if (VEC % 2 == 0 && a.table_vec4) {
 #pragma unroll
@@ -404,7 +427,8 @@ int launch_typed(const RopeArgs& a, cudaStream_t stream, const char* what) {
   if (a.rows >= kWarpKernelMinRows && (MODE == kStore || (a.upv >= 1 && a.upv <= 32))) {
     const int64_t blocks = (a.rows + 7) / 8;  // 8 warps (tokens in flight) per 256-thread block
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(blocks, static_cast<int64_t>(sm_count()) * 16));
-    if (const int launch_status = launch_kernel("rope_kv_warp_kernel", rope_kv_warp_kernel<T, VEC, MODE>, dim3(grid),
+    auto kernel = a.table != nullptr ? rope_kv_warp_kernel<T, VEC, MODE, true> : rope_kv_warp_kernel<T, VEC, MODE, false>;
+    if (const int launch_status = launch_kernel("rope_kv_warp_kernel", kernel, dim3(grid),
                                                 dim3(256), 0, stream, nullptr, a)) {
       return launch_status;
     }
