@@ -362,12 +362,21 @@ __global__ void __launch_bounds__(kCombineThreads) attention_combine_kernel(Attn
   }
   l = combine_block_reduce<kCombineThreads / 32>(l, false, red);  // its barriers also publish w_s
   T* out = static_cast<T*>(a.out) + (b * a.hq + h) * hd;
+  // an empty split writes only its maximum and sum: its output slots hold whatever
+  // the workspace held before, so they are never read, not weighted by 0
   for (int d = tid; d < hd; d += kCombineThreads) {
     float o = 0.f;
-#pragma unroll 4
-    for (int s = 0; s < a.splits; ++s) {
-      // an empty split writes only its maximum and sum: its output slots hold
-      // whatever the workspace held before, so they are skipped, not weighted by 0
+    int s = 0;
+    for (; s + 8 <= a.splits; s += 8) {  // eight splits' loads in flight at once
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = w_s[s + j] != 0.f ? base[(s + j) * split_stride + d] : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (w_s[s + j] != 0.f) o = fmaf(v[j], w_s[s + j], o);
+      }
+    }
+    for (; s < a.splits; ++s) {
       const float w = w_s[s];
       if (w != 0.f) o = fmaf(base[s * split_stride + d], w, o);
     }
