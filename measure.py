@@ -1,7 +1,7 @@
 """Throughput of the tensor-core rows: decode attention and the fused FFN GEMM.
 
-    python -m baremetalinferenceengine_b200.measure attention [--shapes a,b] [--reps 20] [--once]
-    python -m baremetalinferenceengine_b200.measure ffn       [--shapes a,b] [--reps 10] [--once]
+    python measure.py attention [--shapes a,b] [--reps 20] [--once]
+    python measure.py ffn       [--shapes a,b] [--reps 10] [--once]
 
 One JSON line per shape on stdout. Inputs are seeded synthetic tensors of the
 Llama-3 8B / 70B decode and prefill shapes, resident on the GPU. The call is
@@ -25,11 +25,12 @@ import os
 import statistics
 import sys
 
-import torch
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
 
-from . import _lib, ops
+import torch  # noqa: E402
 
-REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+from baremetalinferenceengine_b200 import _lib, ops  # noqa: E402
 FLUSH_BYTES = 256 << 20
 
 # name: (batch, q heads, kv heads, head_dim, max_seq, lengths "full" or "uniform", dtype)

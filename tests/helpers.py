@@ -6,6 +6,8 @@ and the KV-cache copies are bit-exact.
 """
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import torch
 
@@ -48,3 +50,14 @@ def bits_equal(a: torch.Tensor, b: torch.Tensor) -> bool:
     if a.dtype in (torch.float32, torch.int32):
         return torch.equal(a.view(torch.int32), b.view(torch.int32))
     return torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+def reference_dir():
+    """The reference's source checkout, if present: $BM_REFERENCE_DIR, else a
+    `reference` directory beside this repository's. None when neither holds the
+    sources (a GPU host has only the prebuilt checkers under oracle/_ref)."""
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for cand in (os.environ.get("BM_REFERENCE_DIR"), os.path.join(os.path.dirname(repo), "reference")):
+        if cand and os.path.isdir(os.path.join(cand, "src")):
+            return os.path.abspath(cand)
+    return None

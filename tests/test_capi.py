@@ -16,6 +16,7 @@ import tempfile
 import pytest
 
 from baremetalinferenceengine_b200 import _lib, build
+from tests.helpers import reference_dir
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 HEADER = os.path.join(REPO, "include", "bm_layer_ops.h")
@@ -64,14 +65,14 @@ def test_library_exports_the_reference_launch_symbols(lib):
 
 def test_legacy_symbols_match_the_reference_header():
     """Mangle the reference's own declarations with g++ and compare."""
-    ref_header = "/root/reference/include/kernels.cuh"
-    if not os.path.exists(ref_header):
-        pytest.skip("reference header not present")
+    ref = reference_dir()
+    if ref is None:
+        pytest.skip("the reference's sources are not present")
     src = '#include "kernels.cuh"\n' + "\n".join(
         f"void* p_{n} = (void*)&{n};" for n in LEGACY)
     with tempfile.TemporaryDirectory() as tmp:
         obj = os.path.join(tmp, "probe.o")
-        proc = subprocess.run(["g++", "-x", "c++", "-c", "-o", obj, "-I/root/reference/include",
+        proc = subprocess.run(["g++", "-x", "c++", "-c", "-o", obj, f"-I{ref}/include",
                                "-I/usr/local/cuda/include", "-"], input=src.encode(), capture_output=True)
         assert proc.returncode == 0, proc.stderr.decode()
         syms = subprocess.run(["nm", "-u", obj], capture_output=True, text=True).stdout

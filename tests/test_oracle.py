@@ -20,16 +20,16 @@ import pytest
 import torch
 
 from oracle import oracle as orc
-from tests.helpers import from_np, to_np
+from tests.helpers import from_np, reference_dir, to_np
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-REF_SRC = "/root/reference"
 
 
 def _ensure_ref():
     """Builds oracle/_ref from the reference's sources when they are present."""
-    if not orc.ref_available() and os.path.isdir(REF_SRC):
-        subprocess.run(["make", "-s", "-C", os.path.dirname(orc.__file__), "ref"], check=True)
+    ref = reference_dir()
+    if not orc.ref_available() and ref is not None:
+        subprocess.run(["make", "-s", "-C", os.path.dirname(orc.__file__), "ref", f"REF={ref}"], check=True)
     if not orc.ref_available():
         pytest.skip("oracle/_ref is not built and the reference's sources are absent")
 
