@@ -77,18 +77,12 @@ int check_args(const char* what, int64_t batch, int hq, int hkv, int hd, int max
 using namespace attn;
 
 
-int decode_attention(void* out, const void* q, const void* k_cache, const void* v_cache, const int32_t* seq_ids,
-                     const int32_t* lens, int32_t len0, int32_t max_len, int64_t batch, int32_t hq, int32_t hkv,
-                     int32_t hd, int32_t max_seq, int32_t num_seqs, float scale, void* workspace,
-                     size_t workspace_size, bm_dtype_t dtype, int32_t* d_status, void* stream) {
-  const char* what = "bm_decode_attention";
-  if (int st = check_args(what, batch, hq, hkv, hd, max_seq, num_seqs, max_len, dtype)) return st;
-  if (batch == 0) return BM_OK;
-  if (!out || !q || !k_cache || !v_cache) return fail(BM_ERR_INVALID_ARGUMENT, "%s: NULL pointer", what);
-  const int es = dtype_size(dtype);
-  if (!aligned16(k_cache) || !aligned16(v_cache) || (hd * es) % 16 != 0) {
-    return fail(BM_ERR_INVALID_ARGUMENT, "%s: caches must be 16-byte aligned", what);
-  }
+namespace {
+
+// The call's sizes and pointers as the kernels take them (no plan yet).
+AttnArgs fill_args(void* out, const void* q, const void* k_cache, const void* v_cache, const int32_t* seq_ids,
+                   const int32_t* lens, int32_t len0, int32_t max_len, int64_t batch, int32_t hq, int32_t hkv,
+                   int32_t hd, int32_t max_seq, int32_t num_seqs, float scale, int32_t* d_status) {
   if (!(scale > 0.f)) scale = 1.0f / sqrtf(static_cast<float>(hd));
   AttnArgs a{};
   a.out = out;
@@ -105,22 +99,60 @@ int decode_attention(void* out, const void* q, const void* k_cache, const void* 
   a.group = hq / hkv;
   a.max_seq = max_seq;
   a.num_seqs = num_seqs;
+  a.max_len = max_len;
   a.qscale = scale * 1.4426950408889634f;  // scores in base 2: exp(x) = exp2(x * log2(e))
   a.status = d_status;
+  return a;
+}
+
+int check_call(const char* what, void* out, const void* q, const void* k_cache, const void* v_cache, int64_t batch,
+               int32_t hq, int32_t hkv, int32_t hd, int32_t max_seq, int32_t num_seqs, int32_t max_len,
+               bm_dtype_t dtype) {
+  if (int st = check_args(what, batch, hq, hkv, hd, max_seq, num_seqs, max_len, dtype)) return st;
+  if (batch == 0) return BM_OK;
+  if (!out || !q || !k_cache || !v_cache) return fail(BM_ERR_INVALID_ARGUMENT, "%s: NULL pointer", what);
+  const int es = dtype_size(dtype);
+  if (!aligned16(k_cache) || !aligned16(v_cache) || (hd * es) % 16 != 0) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: caches must be 16-byte aligned", what);
+  }
+  return BM_OK;
+}
+
+// CTAs of the balanced kernel: one per SM, no more than there are tiles.
+int balanced_ctas(const AttnArgs& a, int32_t max_len) {
+  const int64_t tiles = a.batch * a.hkv * ((max_len + kThreads - 1) / kThreads);
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(sm_count(), tiles)));
+}
+
+// Fewest tiles a split of the per-pair grid holds on the path these arguments take.
+int grid_min_tiles(const AttnArgs& a, bm_dtype_t dtype) {
+  return tc_eligible(a, dtype) || f32_tma_eligible(a, dtype) ? kStagedMinTiles : kCudaCoreMinTiles;
+}
+
+}  // namespace
+
+int decode_attention(void* out, const void* q, const void* k_cache, const void* v_cache, const int32_t* seq_ids,
+                     const int32_t* lens, int32_t len0, int32_t max_len, int64_t batch, int32_t hq, int32_t hkv,
+                     int32_t hd, int32_t max_seq, int32_t num_seqs, float scale, void* workspace,
+                     size_t workspace_size, bm_dtype_t dtype, int32_t* d_status, void* stream) {
+  const char* what = "bm_decode_attention";
+  if (int st = check_call(what, out, q, k_cache, v_cache, batch, hq, hkv, hd, max_seq, num_seqs, max_len, dtype)) {
+    return st;
+  }
+  if (batch == 0) return BM_OK;
+  AttnArgs a = fill_args(out, q, k_cache, v_cache, seq_ids, lens, len0, max_len, batch, hq, hkv, hd, max_seq,
+                         num_seqs, scale, d_status);
   const bool tc = tc_eligible(a, dtype);
   cudaStream_t s = as_stream(stream);
   if (BM_ATTN_BALANCED && balanced_eligible(a, dtype) && workspace != nullptr &&
       reinterpret_cast<uintptr_t>(workspace) % 16 == 0) {
-    // one CTA per SM, no more than there are tiles
-    const int64_t tiles = batch * hkv * ((max_len + kThreads - 1) / kThreads);
-    const int ctas = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(sm_count(), tiles)));
+    const int ctas = balanced_ctas(a, max_len);
     if (workspace_size >= balanced_workspace_bytes(a.group, ctas)) {
       a.ws = static_cast<float*>(workspace);
       return launch_tc_balanced(a, ctas, s);
     }
   }
-  plan_splits(batch * hkv, max_len, sm_count(), &a.splits, &a.split_len,
-              tc || f32_tma_eligible(a, dtype) ? kStagedMinTiles : kCudaCoreMinTiles);
+  plan_splits(batch * hkv, max_len, sm_count(), &a.splits, &a.split_len, grid_min_tiles(a, dtype));
   const size_t need = workspace_bytes(batch, hkv, a.group, hd, a.splits);
   if (need > 0 && (workspace == nullptr || workspace_size < need)) {
     // Less scratch than the plan wants: as many splits as it holds (maybe one).
@@ -135,6 +167,28 @@ int decode_attention(void* out, const void* q, const void* k_cache, const void* 
   if (tc) return launch_tc(a, s);
   if (f32_tma_eligible(a, dtype)) return launch_f32_tma(a, s);
   return dtype == BM_F32 ? launch_f32(a, s) : launch_bf16(a, s);
+}
+
+int decode_attention_scratch_need(const void* q, const void* k_cache, const void* v_cache, int32_t max_len,
+                                  int64_t batch, int32_t hq, int32_t hkv, int32_t hd, int32_t max_seq,
+                                  int32_t num_seqs, bm_dtype_t dtype, size_t* grid_bytes, size_t* balanced_bytes) {
+  const char* what = "bm_decode_attention_static_scratch";
+  *grid_bytes = *balanced_bytes = 0;
+  // the output pointer is not known here and not needed for the plan: q stands in
+  if (int st = check_call(what, const_cast<void*>(q), q, k_cache, v_cache, batch, hq, hkv, hd, max_seq, num_seqs,
+                          max_len, dtype)) {
+    return st;
+  }
+  if (batch == 0) return BM_OK;
+  const AttnArgs a = fill_args(nullptr, q, k_cache, v_cache, nullptr, nullptr, 0, max_len, batch, hq, hkv, hd,
+                               max_seq, num_seqs, 0.f, nullptr);
+  int splits = 1, split_len = 0;
+  plan_splits(batch * hkv, max_len, sm_count(), &splits, &split_len, grid_min_tiles(a, dtype));
+  *grid_bytes = workspace_bytes(batch, hkv, a.group, hd, splits);
+  *balanced_bytes = BM_ATTN_BALANCED && balanced_eligible(a, dtype)
+                        ? balanced_workspace_bytes(a.group, balanced_ctas(a, max_len))
+                        : SIZE_MAX;
+  return BM_OK;
 }
 
 size_t decode_attention_workspace(int64_t batch, int32_t hq, int32_t hkv, int32_t hd, int32_t max_len) {

@@ -28,6 +28,7 @@ struct AttnArgs {
   int32_t len0;
   int64_t batch;
   int hq, hkv, hd, group, max_seq, num_seqs;
+  int max_len;            // the caller's bound on every query's length (plans cover it)
   int splits, split_len;  // positions per split (a multiple of kThreads)
   float qscale;           // log2(e) * softmax scale
   float* ws;              // [batch][hkv][splits][group][hd + 2]: o..., m, l
@@ -36,13 +37,15 @@ struct AttnArgs {
 
 __device__ __forceinline__ int query_len(const AttnArgs& a, int64_t b) { return a.lens ? a.lens[b] : a.len0; }
 
-// Returns the query's status bits (0 = valid).
+// Returns the query's status bits (0 = valid). A length above the caller's
+// max_len is flagged on every path: the split plans only cover max_len
+// positions, so such a query would otherwise lose its last positions silently.
 __device__ __forceinline__ int32_t check_query(const AttnArgs& a, int64_t b, int* seq, int* len) {
   *seq = a.seq_ids ? a.seq_ids[b] : 0;
   *len = query_len(a, b);
   int32_t bad = 0;
   if (*seq < 0 || *seq >= a.num_seqs) bad |= BM_DEVERR_BAD_SEQUENCE;
-  if (*len <= 0 || *len > a.max_seq) bad |= BM_DEVERR_BAD_POSITION;
+  if (*len <= 0 || *len > a.max_seq || *len > a.max_len) bad |= BM_DEVERR_BAD_POSITION;
   return bad;
 }
 

@@ -7,7 +7,10 @@
 // sequence and uploads the (position, sequence) pairs from a pinned staging
 // buffer into two device arrays that bm_rope_kv_store reads. An event guards
 // the staging buffer, so an append never overwrites values a previous upload is
-// still reading. Not thread-safe: one host thread drives one cache.
+// still reading. The device arrays themselves are rewritten by every append, so
+// appends and the kernels that read their arrays must share one stream (stream
+// order keeps an upload behind the previous step's readers). Not thread-safe: one
+// host thread drives one cache.
 #include <algorithm>
 #include <cstring>
 #include <new>

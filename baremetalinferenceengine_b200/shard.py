@@ -29,6 +29,31 @@ def strong_rows(rank: int, world: int, total_rows: int) -> range:
     return range(start, min(total_rows, start + block))
 
 
+def local_shape(shape, rank: int, world: int, scaling: str = "strong"):
+    """This rank's share of a layer-step workload: (shape with this rank's rows
+    and sequences, global row range).
+
+    strong: the workload's rows split into contiguous blocks of ceil(R/world);
+            the cache holds only the sequences those rows touch (a sequence cut
+            between ranks keeps its positions: each rank writes its own slots).
+    weak:   every rank owns a whole copy of the workload's rows (an N x R job).
+    """
+    import dataclasses
+
+    if scaling == "weak":
+        rows = weak_rows(rank, world, shape.rows)
+        return shape, rows
+    if scaling != "strong":
+        raise ValueError(f"scaling must be 'strong' or 'weak', got {scaling!r}")
+    rows = strong_rows(rank, world, shape.rows)
+    n = len(rows)
+    if shape.positions == "tiled":
+        seqs = (-(-rows.stop // shape.max_seq) - rows.start // shape.max_seq) if n else 1
+    else:
+        seqs = max(1, min(shape.num_seqs, n))
+    return dataclasses.replace(shape, rows=n, num_seqs=max(1, seqs)), rows
+
+
 def max_over_ranks(values: Sequence[float], device=None) -> list:
     """Element-wise MAX of `values` over all ranks (identity without a process group)."""
     import torch

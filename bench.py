@@ -61,7 +61,12 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(OP_ROWS), default="llama70b_bf16",
                     help="a layer-step workload (default) or one of the tensor-core op rows")
-    ap.add_argument("--rows", type=int, default=0, help="override tokens per GPU")
+    ap.add_argument("--rows", type=int, default=0, help="override the workload's tokens")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="strong: the workload's tokens split across the GPUs (default); weak: every GPU its own copy")
+    ap.add_argument("--no-parity", action="store_true", help="skip the sampled-row oracle check after timing")
+    ap.add_argument("--no-ref-gpu", action="store_true", help="skip timing the reference's CUDA kernels")
+    ap.add_argument("--ref-gpu-rows", type=int, default=256, help="tokens of the reference-kernel sample")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--e2e-chunks", type=int, default=16)
     ap.add_argument("--no-e2e", action="store_true")
@@ -296,10 +301,10 @@ def run_reference(args, shape):
               f"RoPE+KV store, add+RMSNorm, SwiGLU), oracle_layer_step_mt on {threads} threads")
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": K, "warmup": W,
-        "ms_per_step": round(elapsed / K * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(elapsed / K * 1e3, 3), "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": "bf16" if shape.es == 2 else "f32", "data": "synthetic (seeded N(0,1))",
         "impl": "reference",
-        "config": config_dict(shape, args.gpus),
+        "config": config_dict(shape, args.gpus, args.scaling, shard_of(shape, args)),
         "rows_per_s": round(rows * K / elapsed, 1),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
@@ -309,16 +314,30 @@ def run_reference(args, shape):
     return 0
 
 
-def config_dict(shape, n):
-    return {"workload": shape.name, "description": shape.description, "rows_per_gpu": shape.rows,
-            "global_rows": shape.rows * n, "dim": shape.dim, "q_heads": shape.hq, "kv_heads": shape.hkv,
-            "head_dim": shape.hd, "ffn": shape.ffn, "vocab": shape.vocab, "rope_theta": shape.theta,
-            "max_seq": shape.max_seq, "sequences_per_gpu": shape.num_seqs,
-            "l2": f"inputs larger than L2: {shape.step_bytes() / 1e9:.2f} GB moved per step vs 126 MB L2"
-                  if shape.step_bytes() >= L2_RESIDENT_BYTES else
+def shard_of(shape, args):
+    """Rank 0's share of the workload (its config entry), without a process group."""
+    from baremetalinferenceengine_b200 import shard
+
+    return shard.local_shape(shape, 0, max(1, args.gpus), args.scaling)[0]
+
+
+def config_dict(shape, n, scaling="weak", local=None):
+    """The workload `shape` (the whole job's tokens for strong scaling, each GPU's
+    for weak) and this rank's share `local`."""
+    local = local or shape
+    strong = scaling == "strong"
+    return {"workload": shape.name, "description": shape.description, "rows_per_gpu": local.rows,
+            "global_rows": shape.rows if strong else shape.rows * n, "dim": shape.dim, "q_heads": shape.hq,
+            "kv_heads": shape.hkv, "head_dim": shape.hd, "ffn": shape.ffn, "vocab": shape.vocab,
+            "rope_theta": shape.theta, "max_seq": shape.max_seq, "sequences": shape.num_seqs * (1 if strong else n),
+            "sequences_per_gpu": local.num_seqs,
+            "l2": f"inputs larger than L2: {local.step_bytes() / 1e9:.2f} GB moved per step per GPU vs 126 MB L2"
+                  if local.step_bytes() >= L2_RESIDENT_BYTES else
                   "L2-resident working set: the step is one CUDA graph replayed after a 256 MB write that "
                   "flushes L2; per-kernel times are per launch of a 16-launch graph (L2 warm)",
-            "parallelism": f"rows{n}: tokens partitioned across {n} GPU(s), no collectives"}
+            "parallelism": (f"rows{n}: the job's {shape.rows} tokens split into {n} contiguous block(s) of "
+                            f"ceil({shape.rows}/{n}) = {-(-shape.rows // n)}, one per GPU, no collectives")
+            if strong else f"rows{n}: every GPU its own {shape.rows} tokens (weak scaling), no collectives"}
 
 
 # ----------------------------------------------------------------------------- op rows
@@ -640,11 +659,15 @@ def main() -> int:
     K, W = args.steps, args.warmup
     if W < 3:
         log("warning: fewer than 3 warm-up steps")
-    log(f"[rank {rank}] allocating {shape.name}: {shape.rows} tokens, {shape.step_bytes() / 1e9:.2f} GB per step")
-    rows = shard.weak_rows(rank, world, shape.rows)  # this rank's tokens of the N x R job
-    b = layer.LayerBuffers(shape, dev, seed=1000 + rank, row_offset=rows.start)
+    affinity = numa_affinity(dev, local_rank, world)  # before any pinned host allocation
+    local, rows = shard.local_shape(shape, rank, world, args.scaling)
+    job_bytes = shape.step_bytes() * (world if args.scaling == "weak" else 1)
+    job_rows = shape.rows * (world if args.scaling == "weak" else 1)
+    log(f"[rank {rank}] allocating {local.name}: tokens [{rows.start}, {rows.stop}) of {job_rows}, "
+        f"{local.step_bytes() / 1e9:.2f} GB per step")
+    b = layer.LayerBuffers(local, dev, seed=1000 + rank, row_offset=rows.start)
     stream = torch.cuda.Stream(dev)
-    kernels = shape.step_kernels()
+    kernels = local.step_kernels()
     nk = len(kernels)
 
     with torch.cuda.stream(stream):
@@ -653,7 +676,8 @@ def main() -> int:
     stream.synchronize()
     assert b.status.read(stream) == 0, "device status set during warm-up"
 
-    small = shape.step_bytes() < L2_RESIDENT_BYTES
+    # the same timing branch on every rank: decided by the largest rank's block
+    small = shape.with_rows(-(-job_rows // world)).step_bytes() < L2_RESIDENT_BYTES
     launches = 0
     if not small:
         # Inputs far larger than L2: K back-to-back steps, events between launches.
@@ -720,10 +744,13 @@ def main() -> int:
     assert b.status.read(stream) == 0, "device status set during the timed steps"
     res = max_over_ranks([elapsed_ms] + per_kernel)
     elapsed_ms, per_kernel = res[0], res[1:]
+    # ---- after the timed region: one more step, its sampled rows checked by the oracle
+    parity = None if args.no_parity else sampled_parity(b, stream, rank)
+    if parity is not None:
+        parity["all_ranks_ok"] = max_over_ranks([0.0 if parity["ok"] else 1.0])[0] == 0.0
 
     peak, peak_kind = measured_peak()
-    step_bytes = shape.step_bytes()
-    value = world * step_bytes * K / (elapsed_ms / 1e3) / 1e9
+    value = job_bytes * K / (elapsed_ms / 1e3) / 1e9
     kern = {}
     for (name, nbytes), ms in zip(kernels, per_kernel):
         gbs = nbytes / (ms / 1e3) / 1e9
@@ -740,19 +767,28 @@ def main() -> int:
 
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": round(elapsed_ms / K, 4), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(elapsed_ms / K, 4), "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": "bf16" if shape.es == 2 else "f32",
         "data": "synthetic: seeded N(0,1) activations, 1+N(0,0.02) norm weights, N(0,0.02) embeddings",
-        "impl": "ours", "config": config_dict(shape, world),
-        "rows_per_s": round(world * shape.rows * K / (elapsed_ms / 1e3), 1),
+        "impl": "ours", "config": config_dict(shape, world, args.scaling, local),
+        "rows_per_s": round(job_rows * K / (elapsed_ms / 1e3), 1),
         "frac_of_peak": round(value / world / peak, 4),
         "kernels": kern, "roofline": roofline, "gpu_launches": launches,
         "clocks": clocks.summary() if rank == 0 else None,
+        "parity_sampled": None if parity is None else parity["all_ranks_ok"],
+        "host_affinity": affinity,
     }
+    if parity is not None:
+        line["parity_detail"] = {k: parity[k] for k in ("rows", "tolerance", "worst_error", "bit_exact", "how")}
 
     # ---- end to end: inputs from pinned host memory, outputs back, every step
     if not args.no_e2e:
-        line["e2e"] = e2e(args, b, shape, dev, world, barrier, max_over_ranks)
+        line["e2e"] = e2e(args, b, local, dev, world, barrier, max_over_ranks)
+    # ---- the reference's own CUDA kernels, one token per launch (rank 0, one GPU only)
+    if world == 1 and not args.no_ref_gpu:
+        del b
+        torch.cuda.empty_cache()
+        line["ref_gpu_baseline"] = ref_gpu_baseline(shape, dev, args.ref_gpu_rows, line["rows_per_s"])
     # ---- CPU baseline (rank 0, one GPU only)
     if world == 1 and not args.no_cpu_baseline:
         threads = host_threads()
@@ -786,9 +822,165 @@ def load_traffic(workload: str, kernel: str):
         return None
 
 
-def pcie_link(dev, h2d, d2h, nbytes: int = 1 << 30, reps: int = 3) -> dict:
-    """Host<->device bandwidth of pinned copies (the roofline of the e2e leg):
-    H2D alone, D2H alone, and both directions at once on two streams."""
+def numa_affinity(dev, local_rank: int, world: int) -> dict:
+    """Binds this process to host CPUs next to its GPU before any pinned host
+    memory is allocated, so the pinned pages land on the GPU's NUMA node
+    (first touch). Ranks whose GPUs share a CPU list split it evenly. Reads
+    sysfs only; returns what it did."""
+    import torch
+
+    def gpu_cpus(index):
+        props = torch.cuda.get_device_properties(index)
+        bus = f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        base = f"/sys/bus/pci/devices/{bus}"
+        with open(f"{base}/local_cpulist") as f:
+            text = f.read().strip()
+        try:
+            with open(f"{base}/numa_node") as f:
+                node = int(f.read().strip())
+        except (OSError, ValueError):
+            node = -1
+        cpus = []
+        for part in text.split(","):
+            lo, _, hi = part.partition("-")
+            cpus.extend(range(int(lo), int(hi or lo) + 1))
+        return bus, node, cpus
+
+    try:
+        allowed = set(os.sched_getaffinity(0))
+        n_local = torch.cuda.device_count()
+        lists = [gpu_cpus(i) for i in range(n_local)]
+        bus, node, cpus = lists[dev.index]
+        sharing = [i for i in range(min(n_local, world)) if lists[i][2] == cpus]
+        cpus = [c for c in cpus if c in allowed] or sorted(allowed)
+        if dev.index in sharing and len(sharing) > 1:
+            k, n = sharing.index(dev.index), len(sharing)
+            share = cpus[k * len(cpus) // n:(k + 1) * len(cpus) // n] or cpus
+        else:
+            share = cpus
+        os.sched_setaffinity(0, share)
+        return {"gpu_pci": bus, "numa_node": node, "cpus": len(share),
+                "cpu_range": f"{min(share)}-{max(share)}", "ranks_sharing_node": len(sharing)}
+    except (OSError, ValueError, AttributeError, IndexError, RuntimeError) as e:
+        return {"unavailable": f"{type(e).__name__}: {e}"}
+
+
+def sampled_parity(b, stream, rank: int) -> dict:
+    """The oracle as the checker, after the timed region: one more step on the same
+    buffers, then the outputs at sampled rows (the first and last, either side of
+    every kernel's first grid-stride wrap, the row holding SwiGLU element 2^31, and
+    8 seeded rows) compared with the oracle within the stated tolerance."""
+    import torch
+
+    from baremetalinferenceengine_b200 import layer
+    from oracle import check_step
+
+    sm = torch.cuda.get_device_properties(b.device).multi_processor_count
+    rows = check_step.sample_rows(b.shape, sm, random_rows=8, seed=100 + rank)
+    sample = check_step.StepSample(b, rows)
+    layer.run_step(b, stream)
+    stream.synchronize()
+    status = b.status.read(stream)
+    res = sample.check()
+    res["ok"] = bool(res["ok"] and status == 0)
+    res["how"] = (f"one untimed step after the timed region; {res['rows']} sampled rows per GPU against the oracle "
+                  f"(oracle/check_step.py), worst |got - want| / (1 + |want|) per output")
+    return res
+
+
+def ref_gpu_baseline(shape, dev, max_rows: int, our_rows_per_s: float) -> dict:
+    """The reference's own CUDA kernels (src/kernels.cu built for sm_100a into
+    oracle/_ref/libref_kernels.so) on this GPU, issued one token at a time as
+    ExecutionEngine::run_layers issues them (ref_layer_step_rows): fp32 buffers of
+    the workload's dims, the first `max_rows` tokens. Timed with CUDA events on the
+    default stream the reference launches on; median of 3 repetitions."""
+    import dataclasses
+
+    import torch
+
+    from oracle import oracle as orc
+
+    if not os.path.exists(orc.REF_KERNELS_LIB):
+        return {"unavailable": "oracle/_ref/libref_kernels.so is not built (needs the reference's sources)"}
+    L = ctypes.CDLL(orc.REF_KERNELS_LIB)
+    vp, i32, i64, f32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
+    L.ref_layer_step_rows.restype = i64
+    L.ref_layer_step_rows.argtypes = [ctypes.c_int, i64, vp, vp, vp] + [vp] * 18 + [ctypes.c_int] * 6 + [f32, f32]
+    s32 = dataclasses.replace(shape, dtype=torch.float32)
+    n = min(shape.rows, max_rows)
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)
+    rnd = lambda *size: torch.randn(*size, generator=g, device=dev)  # noqa: E731
+    ids = torch.randint(0, shape.vocab, (n,), generator=g, device=dev, dtype=torch.int32).cpu()
+    if shape.positions == "uniform":
+        pos = torch.randint(0, shape.max_seq, (n,), generator=g, device=dev, dtype=torch.int32).cpu()
+        seq = (torch.arange(n, dtype=torch.int32) % shape.num_seqs)
+    else:
+        r = torch.arange(n, dtype=torch.int64)
+        pos, seq = (r % shape.max_seq).to(torch.int32), (r // shape.max_seq).to(torch.int32)
+    nseq = int(seq.max()) + 1
+    D, F = shape.dim, shape.ffn
+    t = {"embed": rnd(shape.vocab, D) * 0.02, "hidden": torch.empty(n, D, device=dev), "attn_out": rnd(n, D),
+         "w_attn": rnd(D) * 0.02 + 1, "y_attn": torch.empty(n, D, device=dev), "q": rnd(n, shape.hq, shape.hd),
+         "k": rnd(n, shape.hkv, shape.hd), "v": rnd(n, shape.hkv, shape.hd),
+         "k_cache": torch.zeros(nseq, shape.hkv, shape.max_seq, shape.hd, device=dev),
+         "v_cache": torch.zeros(nseq, shape.hkv, shape.max_seq, shape.hd, device=dev), "ffn_out": rnd(n, D),
+         "w_ffn": rnd(D) * 0.02 + 1, "y_ffn": torch.empty(n, D, device=dev), "gate": rnd(n, F), "up": rnd(n, F),
+         "act": torch.empty(n, F, device=dev)}
+    order = ["embed", "hidden", "attn_out", "w_attn", "y_attn", "q", "k", "v", "k_cache", "v_cache", "ffn_out",
+             "w_ffn", "y_ffn", "gate", "up", "act"]
+    ptrs = [t[k].data_ptr() for k in order]
+    default = torch.cuda.default_stream(dev)
+    torch.cuda.synchronize(dev)
+
+    def run(ops):
+        return L.ref_layer_step_rows(ops, n, ids.data_ptr(), pos.data_ptr(), seq.data_ptr(), *ptrs, D, shape.hq,
+                                     shape.hkv, shape.hd, F, shape.max_seq, shape.theta, shape.eps)
+
+    def timed(ops):
+        run(ops)  # warm
+        ms = []
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(default)
+            issued = run(ops)
+            e1.record(default)
+            torch.cuda.synchronize(dev)
+            ms.append(e0.elapsed_time(e1))
+        return statistics.median(ms), issued
+
+    per_row = s32.bytes_per_row()
+    op_bits = {"embed_gather": (1, per_row["embed_gather"]), "add_rmsnorm_attn": (2, per_row["add_rmsnorm"]),
+               "rope_kv_store": (4, per_row["rope_kv_store"]), "add_rmsnorm_ffn": (8, per_row["add_rmsnorm"]),
+               "swiglu": (16, per_row["swiglu"])}
+    if shape.kind == "stress":
+        op_bits = {k: op_bits[k] for k in ("embed_gather", "swiglu")}
+    per_op = {}
+    for name, (bit, nbytes) in op_bits.items():
+        ms, _ = timed(bit)
+        per_op[name] = {"rows_per_s": round(n / (ms / 1e3), 1), "gbs": round(nbytes * n / (ms / 1e3) / 1e9, 2),
+                        "us_per_row": round(ms * 1e3 / n, 2)}
+    all_ops = sum(bit for bit, _ in op_bits.values())
+    ms, issued = timed(all_ops)
+    step_bytes = sum(nb for _, nb in op_bits.values()) * n
+    rows_per_s = n / (ms / 1e3)
+    del t
+    torch.cuda.empty_cache()
+    return {"value": round(step_bytes / (ms / 1e3) / 1e9, 3), "unit": "GB/s", "rows_per_s": round(rows_per_s, 1),
+            "dtype": "f32", "launches_per_row": issued // n, "per_op": per_op,
+            "ours_over_reference_rows_per_s": round(our_rows_per_s / rows_per_s, 1),
+            "kind": "reference CUDA kernels (src/kernels.cu, sm_100a), one token per launch as "
+                    "ExecutionEngine::run_layers issues them",
+            "sample": f"the first {n} of {shape.rows} tokens of {shape.name} at its dims in fp32 (the reference's "
+                      f"kernels are fp32 only; ours run {('bf16' if shape.es == 2 else 'f32')}), CUDA events on "
+                      f"the default stream, median of 3"}
+
+
+def pcie_link(dev, h2d, d2h, barrier, max_over_ranks, world: int, nbytes: int = 1 << 30, reps: int = 3) -> dict:
+    """Host<->device bandwidth of pinned copies, the roofline of the e2e leg: H2D
+    alone, D2H alone, and both directions at once on two streams. Every rank
+    copies at the same time (a barrier before each phase), so the per-GPU rates
+    are those each GPU gets while all N copy: the host side is shared."""
     import torch
 
     host_a = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
@@ -797,27 +989,35 @@ def pcie_link(dev, h2d, d2h, nbytes: int = 1 << 30, reps: int = 3) -> dict:
     dev_b = torch.empty(nbytes, dtype=torch.uint8, device=dev)
 
     def timed(streams_ops):
+        barrier()
+        torch.cuda.synchronize(dev)
         evs = []
-        for s, op in streams_ops:
+        for st, op in streams_ops:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            with torch.cuda.stream(s):
-                e0.record(s)
+            with torch.cuda.stream(st):
+                e0.record(st)
                 for _ in range(reps):
                     op()
-                e1.record(s)
+                e1.record(st)
             evs.append((e0, e1))
         torch.cuda.synchronize(dev)
-        return max(e0.elapsed_time(e1) for e0, e1 in evs) / 1e3
+        own = max(e0.elapsed_time(e1) for e0, e1 in evs) / 1e3
+        return own, max_over_ranks([own])[0]
 
     up = lambda: dev_a.copy_(host_a, non_blocking=True)  # noqa: E731
     down = lambda: host_b.copy_(dev_b, non_blocking=True)  # noqa: E731
     timed([(h2d, up), (d2h, down)])  # warm
-    t_up = timed([(h2d, up)])
-    t_down = timed([(d2h, down)])
-    t_both = timed([(h2d, up), (d2h, down)])
+    t_up, t_up_all = timed([(h2d, up)])
+    t_down, t_down_all = timed([(d2h, down)])
+    t_both, t_both_all = timed([(h2d, up), (d2h, down)])
     gb = nbytes * reps / 1e9
+    del host_a, host_b, dev_a, dev_b
     return {"h2d_gbs": round(gb / t_up, 1), "d2h_gbs": round(gb / t_down, 1),
-            "bidirectional_gbs": round(2 * gb / t_both, 1), "how": "pinned 1 GiB copies x3, CUDA events"}
+            "bidirectional_gbs": round(2 * gb / t_both, 1),
+            "aggregate": {"h2d_gbs": round(world * gb / t_up_all, 1), "d2h_gbs": round(world * gb / t_down_all, 1),
+                          "bidirectional_gbs": round(2 * world * gb / t_both_all, 1), "gpus": world},
+            "how": f"pinned 1 GiB copies x{reps} per GPU, all {world} GPU(s) at once, CUDA events; per-GPU rates "
+                   f"are this GPU's own, aggregate = all GPUs' bytes / the slowest GPU's time"}
 
 
 def bytes_per_row(b, names) -> float:
@@ -827,7 +1027,10 @@ def bytes_per_row(b, names) -> float:
 def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
     """The same step through the public API with host buffers: every step copies
     its inputs in from pinned host memory and its outputs back, chunked over rows
-    so copies in both directions overlap the kernels of other chunks."""
+    so copies in both directions overlap the kernels of other chunks. Its
+    roofline is the host link measured with every GPU copying at once: a step
+    cannot end before its H2D bytes, its D2H bytes and their sum have crossed at
+    the measured H2D, D2H and bidirectional rates."""
     import torch
 
     from baremetalinferenceengine_b200 import layer
@@ -900,16 +1103,28 @@ def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
     torch.cuda.synchronize(dev)
     barrier()
     ms = max_over_ranks([t0.elapsed_time(t1)])[0]
-    link = pcie_link(dev, h2d, d2h)
-    gbs = world * shape.with_rows(R).step_bytes() * E / (ms / 1e3) / 1e9
-    h2d_rate = bytes_per_row(b, names_in) * R / (ms / E / 1e3) / 1e9
-    return {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": int(bytes_per_row(b, names_in) * R),
-            "d2h_bytes_per_step": int(bytes_per_row(b, names_out) * R), "rows_per_step": R, "steps": E,
-            "ms_per_step": round(ms / E, 4), "chunks": len(slices),
+    del h_in, h_out
+    link = pcie_link(dev, h2d, d2h, barrier, max_over_ranks, world)
+    step_bytes = shape.with_rows(R).step_bytes()
+    gbs = world * step_bytes * E / (ms / 1e3) / 1e9
+    bin_, bout = bytes_per_row(b, names_in) * R, bytes_per_row(b, names_out) * R
+    h2d_rate = bin_ / (ms / E / 1e3) / 1e9
+    # host-side lower bound of one step on this GPU while every GPU copies, then the job's
+    t_link = max(bin_ / (link["h2d_gbs"] * 1e9), bout / (link["d2h_gbs"] * 1e9),
+                 (bin_ + bout) / (link["bidirectional_gbs"] * 1e9))
+    t_link = max_over_ranks([t_link])[0]
+    roof = world * step_bytes / t_link / 1e9
+    return {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": int(bin_), "d2h_bytes_per_step": int(bout),
+            "rows_per_step": R, "steps": E, "ms_per_step": round(ms / E, 4), "chunks": len(slices),
             "link": link, "h2d_gbs_achieved": round(h2d_rate, 1),
-            "frac_of_link": round(h2d_rate / link["h2d_gbs"], 3) if link.get("h2d_gbs") else None,
+            "host_gbs_achieved": round(world * (bin_ + bout) / (ms / E / 1e3) / 1e9, 1),
+            "roofline": {"gbs": round(roof, 2), "ms_per_step": round(t_link * 1e3, 3),
+                         "how": "max over GPUs of max(H2D bytes / H2D rate, D2H bytes / D2H rate, both / "
+                                "bidirectional rate), the rates measured with all GPUs copying at once"},
+            "frac_of_link": round(gbs / roof, 3),
             "how": "per step: pinned-host -> device copies of every input, the five kernels, device -> pinned-host "
-                   "copies of every output, chunked over rows on three streams; CUDA events, max over ranks"}
+                   "copies of every output, chunked over rows on three streams; CUDA events, max over ranks; host "
+                   "buffers pinned after binding the rank to its GPU's NUMA-local CPUs"}
 
 
 if __name__ == "__main__":

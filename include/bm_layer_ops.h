@@ -201,7 +201,8 @@ int bm_kv_store(void* cache, const void* src, const int32_t* positions,
  * `workspace` (caller-owned; its contents need no initialisation). With less
  * scratch than that (or NULL) each (query, kv head) runs unsplit in one CTA:
  * same results, less parallelism. A query with an out-of-range sequence or a
- * length outside [1, max_seq] is skipped and flags *d_status. */
+ * length outside [1, max_len] (max_len <= max_seq) is skipped and flags
+ * *d_status. */
 int bm_decode_attention_workspace_size(int64_t batch, int32_t num_q_heads, int32_t num_kv_heads,
                                        int32_t head_dim, int32_t max_len, size_t* bytes_out);
 int bm_decode_attention(void* out, const void* q, const void* k_cache, const void* v_cache,
@@ -216,10 +217,12 @@ int bm_decode_attention(void* out, const void* q, const void* k_cache, const voi
  * that cannot afford cudaMalloc's implicit synchronisation). No counterpart in
  * the reference. Same arguments and results as bm_decode_attention, without the
  * workspace: the split partials live in an 8 MiB array compiled into the
- * library (one copy per GPU, held until the process exits). A batch whose split
- * plan needs more than 8 MiB (bm_decode_attention_workspace_size) is rejected
- * with BM_ERR_INVALID_ARGUMENT. The first call on a device looks up that
- * device's copy of the array; make it before capturing any stream. All calls
+ * library (one copy per GPU, held until the process exits). Arguments are
+ * checked as bm_decode_attention checks them; then a batch whose split plan
+ * (the one bm_decode_attention runs with a workspace of this array's size)
+ * needs more than 8 MiB is rejected with BM_ERR_INVALID_ARGUMENT. The first
+ * call in a CUDA context looks up that context's copy of the array (cached under
+ * the context's unique id); make it before capturing any stream. All calls
  * share the array: calls that overlap on the GPU race on it and must be
  * serialised by the caller. */
 int bm_decode_attention_static_scratch(void* out, const void* q, const void* k_cache, const void* v_cache,
@@ -283,7 +286,10 @@ int bm_softmax(void* x, int64_t size, int64_t num_vectors, int64_t stride, bm_dt
  * returns their device pointers for bm_rope_kv_store. It fails, changing
  * nothing, if a sequence would pass max_seq or rows exceeds max_tokens.
  * The host copy is synchronous with respect to the host buffer (the call
- * returns after the upload is queued from the cache's own pinned staging). */
+ * returns after the upload is queued from the cache's own pinned staging).
+ * Every append overwrites the same two device arrays, so issue each append and
+ * the bm_rope_kv_store calls that read its arrays on one stream: stream order
+ * then keeps the next append's upload behind the previous step's readers. */
 typedef struct bm_kv_cache bm_kv_cache_t;
 
 int bm_kv_cache_create(int32_t num_layers, int32_t num_seqs, int32_t num_kv_heads, int32_t max_seq,

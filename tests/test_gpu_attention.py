@@ -32,11 +32,12 @@ def oracle_attention(q, kc, vc, seq_ids, lens):
     return out, bad
 
 
-def run(cuda, q, kc, vc, seq_ids, lens, workspace=True, status=None):
+def run(cuda, q, kc, vc, seq_ids, lens, workspace=True, status=None, max_len=None):
     batch, hq, hd = q.shape
     num_seqs, hkv, max_seq, _ = kc.shape
     L = _lib.load()
-    max_len = int(lens.max()) if lens.numel() else 1
+    if max_len is None:
+        max_len = int(lens.max()) if lens.numel() else 1
     need = ctypes.c_size_t()
     _lib.check(L.bm_decode_attention_workspace_size(batch, hq, hkv, hd, max_len, ctypes.byref(need)))
     ws = torch.empty(max(need.value, 1), dtype=torch.uint8, device=cuda) if workspace else None
@@ -165,6 +166,34 @@ def test_bad_entries_are_skipped_and_flagged(cuda):
     assert orc.worst_error(outc[0].numpy(), want[0]) <= 1e-5
     for b in (1, 2, 3):
         assert bits_equal(outc[b], torch.full((8, 64), 7.0))
+
+
+@pytest.mark.parametrize("path,dt,batch,hq,hkv,hd", [
+    ("cuda_cores_f32", torch.float32, 4, 8, 2, 64),
+    ("cuda_cores_bf16", torch.bfloat16, 4, 8, 2, 64),
+    ("tensor_cores_per_pair_grid", torch.bfloat16, 4, 8, 2, 128),  # 8 pairs: below the balanced minimum
+    ("tensor_cores_balanced", torch.bfloat16, 8, 8, 8, 128),  # 64 pairs, with a workspace
+    ("f32_tma", torch.float32, 4, 8, 2, 128),
+])
+def test_lengths_beyond_max_len_are_flagged_on_every_path(cuda, path, dt, batch, hq, hkv, hd):
+    """max_len bounds every query's length: the split plans cover max_len
+    positions, so a longer query (still within max_seq) is flagged
+    BM_DEVERR_BAD_POSITION and skipped on every path, never cut short."""
+    g = gen(hd + batch)
+    max_seq, max_len = 2048, 1000
+    q = randn((batch, hq, hd), dt, g)
+    kc, vc = randn((batch, hkv, max_seq, hd), dt, g), randn((batch, hkv, max_seq, hd), dt, g)
+    lens = torch.tensor(([2048, 600, 1000, 1001, 300, 999, 1500, 1][:batch]), dtype=torch.int32)
+    seq_ids = torch.arange(batch, dtype=torch.int32)
+    status = ops.DeviceStatus(cuda)
+    out, _ = run(cuda, q, kc, vc, seq_ids, lens, status=status, max_len=max_len)
+    assert status.read() == _lib.BM_DEVERR_BAD_POSITION
+    ok = lens <= max_len
+    want, _ = oracle_attention(q[ok], kc, vc, seq_ids[ok], lens[ok])
+    outc = out.cpu()
+    assert orc.worst_error(to_np(outc[ok]), want) <= TOL[dt]
+    for b in torch.nonzero(~ok).flatten().tolist():
+        assert bits_equal(outc[b], torch.full((hq, hd), 7.0, dtype=dt)), b
 
 
 def test_workspace_size_and_argument_checks(cuda):

@@ -88,6 +88,41 @@ def _dying_worker(rank, world, port, out_dir):
     os._exit(0)
 
 
+def _strong_worker(rank, world, port, out_dir):
+    """Fixed-total split: each rank builds only its block of the job's tokens;
+    together the ranks write every (sequence, position) slot exactly once."""
+    import dataclasses
+
+    _init(rank, world, port, 60)
+    job = dataclasses.replace(WORKLOADS["llama70b_bf16"], rows=1024, dim=32, hq=4, hkv=2, hd=8, ffn=16, vocab=64,
+                              max_seq=256, num_seqs=4, dtype=torch.float32)
+    local, rows = shard.local_shape(job, rank, world, "strong")
+    b = LayerBuffers(local, "cpu", seed=7 + rank, row_offset=rows.start, with_table=False)
+    assert b.q.shape[0] == len(rows) == local.rows
+    assert int(b.seq_ids.max()) < local.num_seqs and int(b.positions.max()) < job.max_seq
+    # back to global slots: the local sequence id is offset by the block's first sequence
+    first_seq = rows.start // job.max_seq
+    mine = [(first_seq + int(s), int(p)) for s, p in zip(b.seq_ids, b.positions)]
+    every = [None] * world
+    dist.all_gather_object(every, mine)
+    slots = [x for part in every for x in part]
+    assert len(slots) == len(set(slots)) == job.rows
+    assert sorted(slots) == [(r // job.max_seq, r % job.max_seq) for r in range(job.rows)]
+    # the parity flag is reduced the way bench.py reduces it: any failing rank fails the job
+    flag = shard.max_over_ranks([1.0 if rank == world - 1 else 0.0])[0]
+    assert flag == 1.0
+    dist.barrier()
+    dist.destroy_process_group()
+    open(os.path.join(out_dir, f"ok{rank}"), "w").close()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gloo_ranks_strong_split_cover_the_job_once(tmp_path, world):
+    mp.start_processes(_strong_worker, args=(world, free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    assert all(os.path.exists(tmp_path / f"ok{r}") for r in range(world))
+
+
 def test_a_dead_rank_is_detected_not_hung(tmp_path):
     ctx = mp.start_processes(_dying_worker, args=(2, free_port(), str(tmp_path)), nprocs=2, start_method="spawn",
                              join=False)
