@@ -29,6 +29,22 @@ BM_DEVERR_BAD_POSITION = 0x2
 BM_DEVERR_BAD_SEQUENCE = 0x4
 BM_DEVERR_TIMEOUT = 0x8
 
+class LayerStepC(ctypes.Structure):
+    """Mirror of bm_layer_step_t (include/bm_layer_ops.h): one layer step's sizes
+    and device buffers."""
+
+    _fields_ = [
+        ("rows", c_int64), ("dim", c_int32), ("ffn", c_int32), ("vocab", c_int64),
+        ("num_q_heads", c_int32), ("num_kv_heads", c_int32), ("head_dim", c_int32), ("max_seq", c_int32),
+        ("num_seqs", c_int32), ("eps", c_float), ("theta", c_double),
+        ("ids", c_void_p), ("embed", c_void_p), ("hidden", c_void_p), ("attn_out", c_void_p), ("w_attn", c_void_p),
+        ("y_attn", c_void_p), ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("positions", c_void_p),
+        ("seq_ids", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p), ("rope_table", c_void_p),
+        ("rope_table_len", c_int32), ("ffn_out", c_void_p), ("w_ffn", c_void_p), ("y_ffn", c_void_p),
+        ("gate", c_void_p), ("up", c_void_p), ("act", c_void_p),
+    ]
+
+
 # name -> (restype, argtypes). Every symbol include/bm_layer_ops.h declares.
 SIGNATURES = {
     "bm_status_string": (c_char_p, [c_int]),
@@ -76,6 +92,7 @@ SIGNATURES = {
     "bm_kv_cache_append": (c_int, [c_void_p, c_void_p, c_int64, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p),
                                    c_void_p]),
     "bm_selftest_bounded_wait": (c_int, [c_int64, c_void_p, c_void_p, c_void_p]),
+    "bm_layer_step": (c_int, [ctypes.POINTER(LayerStepC), c_int, c_void_p, c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -118,6 +118,30 @@ __device__ __forceinline__ void st_stream(void* p, const uint4& v) {
   __stcs(reinterpret_cast<uint4*>(p), v);
 }
 
+// exp(-g) = 2^(-g * log2(e)) with the hardware's ex2.approx, and the reciprocal
+// with rcp.approx (both single MUFU instructions; relative errors near 2^-22).
+// ex2 of a large argument is +inf and rcp(+inf) is +0, so silu(-1000) = -0 and
+// silu(+1000) = 1000 exactly as in the reference's known-answer test
+// (tests/kernel_tests.cu:164-173).
+__device__ __forceinline__ float silu_fast(float g) {
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(g * -1.4426950408889634f));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+  return g * r;
+}
+
+// One SwiGLU element, silu(g) * u (reference swiglu_kernel, src/kernels.cu:185-190):
+// fp32 I/O computes g / (1 + expf(-g)) * u exactly as the reference writes it;
+// bf16 I/O uses silu_fast, whose error is far below bf16 rounding.
+template <typename T>
+__device__ __forceinline__ float swiglu1(float g, float u) {
+  if constexpr (sizeof(T) == 4) {
+    return g / (1.0f + expf(-g)) * u;
+  } else {
+    return silu_fast(g) * u;
+  }
+}
+
 // Butterfly sum: every lane of the warp gets the total.
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

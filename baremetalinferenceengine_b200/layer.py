@@ -48,22 +48,42 @@ class LayerShape:
     def es(self) -> int:
         return 4 if self.dtype == torch.float32 else 2
 
+    @property
+    def fused(self) -> bool:
+        """Whether the step runs as one launch (bm_layer_step's single-launch form:
+        a layer step of at most FUSED_MAX_ROWS tokens)."""
+        return self.kind == "layer" and self.rows <= FUSED_MAX_ROWS
+
     def bytes_per_row(self) -> dict:
         """Algorithmic HBM bytes per token for each kernel: every input element read
         once and every output element written once (weights, the RoPE table and
-        the embedding rows' reuse are not counted)."""
+        the embedding rows' reuse are not counted). layer_step is the single-launch
+        step: the embedding row, both deltas read, y_attn, y_ffn and hidden written
+        once (the residual never round-trips), RoPE + K/V and SwiGLU as above."""
         es = self.es
-        return {
+        b = {
             "embed_gather": 2 * self.dim * es + 4,
             "add_rmsnorm": 4 * self.dim * es,  # read residual + delta, write residual + out
             "rope_kv_store": (2 * self.hq * self.hd + 2 * self.hkv * self.hd + 2 * self.hkv * self.hd) * es + 8,
             "swiglu": 3 * self.ffn * es,
         }
+        b["layer_step"] = 6 * self.dim * es + 4 + b["rope_kv_store"] + b["swiglu"]
+        return b
+
+    def op_bytes(self) -> int:
+        """Algorithmic bytes of the step's five ops as separate kernels (the
+        workload's metric, whichever way the step is launched)."""
+        b = self.bytes_per_row()
+        if self.kind == "stress":
+            return (b["embed_gather"] + b["swiglu"]) * self.rows
+        return (b["embed_gather"] + 2 * b["add_rmsnorm"] + b["rope_kv_store"] + b["swiglu"]) * self.rows
 
     def step_kernels(self) -> list:
         """(kernel, algorithmic bytes per launch) in launch order for one step."""
         b = self.bytes_per_row()
         r = self.rows
+        if self.fused:
+            return [("layer_step", b["layer_step"] * r)]
         if self.kind == "stress":
             return [("embed_gather", b["embed_gather"] * r), ("swiglu", b["swiglu"] * r)]
         return [("embed_gather", b["embed_gather"] * r), ("add_rmsnorm_attn", b["add_rmsnorm"] * r),
@@ -71,11 +91,15 @@ class LayerShape:
                 ("swiglu", b["swiglu"] * r)]
 
     def step_bytes(self) -> int:
-        return sum(n for _, n in self.step_kernels())
+        return self.op_bytes()
 
     def with_rows(self, rows: int) -> "LayerShape":
         return dataclasses.replace(self, rows=rows)
 
+
+# Layer steps of at most this many tokens run as one launch (bm_layer_step; the
+# library's BM_STEP_FUSED_MAX_ROWS).
+FUSED_MAX_ROWS = 512
 
 # Synthetic workloads (seeded; no dataset): the model shapes and token layouts the
 # kernels are measured on.
@@ -198,6 +222,11 @@ def step_launchers(b: LayerBuffers, stream: Optional[torch.cuda.Stream] = None,
     s = b.shape
     sl = rows if rows is not None else slice(0, s.rows)
     st = b.status
+    if s.fused:
+        return [("layer_step", lambda: ops.layer_step(
+            b.ids[sl], b.embed, b.hidden[sl], b.attn_out[sl], b.w_attn, b.y_attn[sl], b.q[sl], b.k[sl], b.v[sl],
+            b.positions[sl], b.k_cache, b.v_cache, b.ffn_out[sl], b.w_ffn, b.y_ffn[sl], b.gate[sl], b.up[sl],
+            b.act[sl], s.eps, table=b.table, theta=s.theta, seq_ids=b.seq_ids[sl], status=st, stream=stream))]
     gather = ("embed_gather", lambda: ops.embed_gather(b.embed, b.ids[sl], out=b.hidden[sl], status=st,
                                                         stream=stream))
     swiglu = ("swiglu", lambda: ops.swiglu(b.gate[sl], b.up[sl], out=b.act[sl], stream=stream))

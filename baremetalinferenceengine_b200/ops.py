@@ -353,6 +353,51 @@ def kv_store(cache: torch.Tensor, src: torch.Tensor, positions, seq_ids: Optiona
 # The reference's launch API (single token, fp32), include/kernels.cuh
 # --------------------------------------------------------------------------
 
+def layer_step(ids: torch.Tensor, embed: torch.Tensor, hidden: torch.Tensor, attn_out: torch.Tensor,
+               w_attn: torch.Tensor, y_attn: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+               positions: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, ffn_out: torch.Tensor,
+               w_ffn: torch.Tensor, y_ffn: torch.Tensor, gate: torch.Tensor, up: torch.Tensor, act: torch.Tensor,
+               eps: float = 1e-5, table: Optional[RopeTable] = None, theta: float = 10000.0,
+               seq_ids: Optional[torch.Tensor] = None, status: Optional[DeviceStatus] = None, stream=None) -> None:
+    """One layer step (bm_layer_step): hidden = embed[ids] + attn_out, y_attn =
+    rmsnorm(hidden) * w_attn, RoPE on q (in place) and k into k_cache with v into
+    v_cache, hidden += ffn_out, y_ffn = rmsnorm(hidden) * w_ffn, act = silu(gate)
+    * up. One launch for batches of at most 512 tokens, five otherwise."""
+    rows, dim = hidden.shape
+    for t, n in ((embed, "embed"), (hidden, "hidden"), (attn_out, "attn_out"), (w_attn, "w_attn"),
+                 (y_attn, "y_attn"), (q, "q"), (k, "k"), (v, "v"), (k_cache, "k_cache"), (v_cache, "v_cache"),
+                 (ffn_out, "ffn_out"), (w_ffn, "w_ffn"), (y_ffn, "y_ffn"), (gate, "gate"), (up, "up"), (act, "act")):
+        _dense(t, n)
+    _same(hidden, embed, attn_out, w_attn, y_attn, q, k, v, k_cache, v_cache, ffn_out, w_ffn, y_ffn, gate, up, act)
+    _i32(ids, "ids")
+    _i32(positions, "positions")
+    _i32(seq_ids, "seq_ids")
+    ffn = gate.shape[-1]
+    shapes_ok = (attn_out.shape == hidden.shape == y_attn.shape == ffn_out.shape == y_ffn.shape
+                 and embed.shape[1] == dim and w_attn.numel() == dim and w_ffn.numel() == dim
+                 and gate.shape == up.shape == act.shape == (rows, ffn) and ids.numel() == rows
+                 and positions.numel() == rows and q.shape[0] == rows and k.shape == v.shape
+                 and k.shape[0] == rows and k_cache.shape == v_cache.shape and k_cache.shape[1] == k.shape[1]
+                 and (seq_ids is None or seq_ids.numel() == rows))
+    if not shapes_ok:
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "layer step tensor shapes disagree")
+    c = _lib.LayerStepC()
+    c.rows, c.dim, c.ffn, c.vocab = rows, dim, ffn, embed.shape[0]
+    c.num_q_heads, c.num_kv_heads, c.head_dim = q.shape[1], k.shape[1], q.shape[2]
+    c.max_seq, c.num_seqs, c.eps, c.theta = k_cache.shape[2], k_cache.shape[0], eps, theta
+    c.ids, c.embed, c.hidden, c.attn_out, c.w_attn, c.y_attn = (_ptr(ids), _ptr(embed), _ptr(hidden), _ptr(attn_out),
+                                                                _ptr(w_attn), _ptr(y_attn))
+    c.q, c.k, c.v, c.positions, c.seq_ids = _ptr(q), _ptr(k), _ptr(v), _ptr(positions), _ptr(seq_ids)
+    c.k_cache, c.v_cache = _ptr(k_cache), _ptr(v_cache)
+    c.rope_table = None if table is None else table.ptr
+    c.rope_table_len = 0 if table is None else table.max_pos
+    c.ffn_out, c.w_ffn, c.y_ffn, c.gate, c.up, c.act = (_ptr(ffn_out), _ptr(w_ffn), _ptr(y_ffn), _ptr(gate),
+                                                        _ptr(up), _ptr(act))
+    with torch.cuda.device(_dev(hidden)):
+        check(load().bm_layer_step(ctypes.byref(c), bm_dtype(hidden), None if status is None else status.ptr,
+                                   _stream(hidden.device, stream)))
+
+
 def _stream_arg(stream) -> int:
     if stream is None or stream == 0:
         return 0

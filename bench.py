@@ -788,7 +788,10 @@ def main() -> int:
     if world == 1 and not args.no_ref_gpu:
         del b
         torch.cuda.empty_cache()
-        line["ref_gpu_baseline"] = ref_gpu_baseline(shape, dev, args.ref_gpu_rows, line["rows_per_s"])
+        try:
+            line["ref_gpu_baseline"] = ref_gpu_baseline(shape, dev, args.ref_gpu_rows, line["rows_per_s"])
+        except (OSError, TypeError, ValueError, RuntimeError) as e:  # a baseline leg never sinks the line
+            line["ref_gpu_baseline"] = {"unavailable": f"{type(e).__name__}: {e}"}
     # ---- CPU baseline (rank 0, one GPU only)
     if world == 1 and not args.no_cpu_baseline:
         threads = host_threads()
@@ -888,6 +891,21 @@ def sampled_parity(b, stream, rank: int) -> dict:
     return res
 
 
+def ref_kernels_lib():
+    """oracle/_ref/libref_kernels.so with ref_layer_step_rows typed, or None when
+    the reference's kernels were not built."""
+    from oracle import oracle as orc
+
+    if not os.path.exists(orc.REF_KERNELS_LIB):
+        return None
+    L = ctypes.CDLL(orc.REF_KERNELS_LIB)
+    vp, i64, f32, ci = ctypes.c_void_p, ctypes.c_int64, ctypes.c_float, ctypes.c_int
+    L.ref_layer_step_rows.restype = i64
+    # ops, rows, ids, positions, seq_ids, 16 device buffers, six sizes, theta, eps
+    L.ref_layer_step_rows.argtypes = [ci, i64, vp, vp, vp] + [vp] * 16 + [ci] * 6 + [f32, f32]
+    return L
+
+
 def ref_gpu_baseline(shape, dev, max_rows: int, our_rows_per_s: float) -> dict:
     """The reference's own CUDA kernels (src/kernels.cu built for sm_100a into
     oracle/_ref/libref_kernels.so) on this GPU, issued one token at a time as
@@ -900,12 +918,9 @@ def ref_gpu_baseline(shape, dev, max_rows: int, our_rows_per_s: float) -> dict:
 
     from oracle import oracle as orc
 
-    if not os.path.exists(orc.REF_KERNELS_LIB):
+    L = ref_kernels_lib()
+    if L is None:
         return {"unavailable": "oracle/_ref/libref_kernels.so is not built (needs the reference's sources)"}
-    L = ctypes.CDLL(orc.REF_KERNELS_LIB)
-    vp, i32, i64, f32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
-    L.ref_layer_step_rows.restype = i64
-    L.ref_layer_step_rows.argtypes = [ctypes.c_int, i64, vp, vp, vp] + [vp] * 18 + [ctypes.c_int] * 6 + [f32, f32]
     s32 = dataclasses.replace(shape, dtype=torch.float32)
     n = min(shape.rows, max_rows)
     g = torch.Generator(device=dev)

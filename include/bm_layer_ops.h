@@ -124,6 +124,60 @@ int bm_swiglu(void* out, const void* gate, const void* up, int64_t n,
               bm_dtype_t dtype, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * One layer step: the five ops above in the order ExecutionEngine::run_layers
+ * issues them for a token (src/execution_engine.cu:98-126), for a batch of
+ * rows, equivalent to
+ *   bm_embed_gather(hidden <- embed[ids])
+ *   bm_add_rmsnorm(hidden += attn_out; y_attn = rmsnorm(hidden) * w_attn)
+ *   bm_rope_kv_store(q in place; rotated k and v into the caches)
+ *   bm_add_rmsnorm(hidden += ffn_out; y_ffn = rmsnorm(hidden) * w_ffn)
+ *   bm_swiglu(act = silu(gate) * up)
+ * No single reference function: it groups the reference's per-token calls.
+ * Batches of at most 512 tokens with 16-byte aligned buffers and whole-vector
+ * rows run as ONE launch (the only dependency between the ops is the row-local
+ * residual, so the launch holds independent row, token and SwiGLU jobs); larger
+ * batches issue the five batched kernels. Results are the same either way (the
+ * residual and the cache copies bit for bit). Every array is row-major and
+ * contiguous: hidden, attn_out, y_attn, ffn_out, y_ffn [rows][dim]; q
+ * [rows][num_q_heads][head_dim]; k, v [rows][num_kv_heads][head_dim]; gate, up,
+ * act [rows][ffn]; caches [num_seqs][num_kv_heads][max_seq][head_dim];
+ * positions and ids int32[rows]; seq_ids int32[rows] or NULL (all 0);
+ * rope_table as for bm_rope_kv_store (NULL: fp64 angles from theta). Bad ids,
+ * positions and sequences flag *d_status and skip that row's op, as the
+ * separate calls do. */
+typedef struct bm_layer_step {
+  int64_t rows;
+  int32_t dim, ffn;
+  int64_t vocab;
+  int32_t num_q_heads, num_kv_heads, head_dim, max_seq, num_seqs;
+  float eps;
+  double theta;
+  const int32_t* ids;
+  const void* embed;
+  void* hidden;
+  const void* attn_out;
+  const void* w_attn;
+  void* y_attn;
+  void* q;
+  const void* k;
+  const void* v;
+  const int32_t* positions;
+  const int32_t* seq_ids;
+  void* k_cache;
+  void* v_cache;
+  const void* rope_table;
+  int32_t rope_table_len;
+  const void* ffn_out;
+  const void* w_ffn;
+  void* y_ffn;
+  const void* gate;
+  const void* up;
+  void* act;
+} bm_layer_step_t;
+
+int bm_layer_step(const bm_layer_step_t* step, bm_dtype_t dtype, int32_t* d_status, void* stream);
+
+/* ---------------------------------------------------------------------------
  * RoPE table: fp32 (cos, sin) pairs laid out [max_pos][head_dim/2], entry
  * (p, i) for angle p / theta^(2i/head_dim), computed on the device in fp64
  * (the angle formula of the reference's CPU check loop,

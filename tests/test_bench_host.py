@@ -46,3 +46,37 @@ def test_strong_split_shapes_and_config():
     pre = WORKLOADS["llama8b_prefill_bf16"]
     p, rows = shard.local_shape(pre, 1, 8, "strong")
     assert (p.rows, p.num_seqs, rows.start) == (4096, 1, 4096)
+
+
+def test_reference_kernel_step_binding():
+    """The ctypes binding of the reference-kernel step (bench.py's GPU baseline
+    leg) matches the C function: a call over zero tokens issues nothing and needs
+    no GPU."""
+    import os
+
+    from oracle import oracle as orc
+
+    if not os.path.exists(orc.REF_KERNELS_LIB):
+        import pytest
+
+        pytest.skip("oracle/_ref/libref_kernels.so is not built")
+    L = bench.ref_kernels_lib()
+    args = [31, 0, None, None, None] + [None] * 16 + [4096, 32, 8, 128, 14336, 8192] + [5e5, 1e-5]
+    assert L.ref_layer_step_rows(*args) == 0
+
+
+def test_run_step_uses_one_launch_for_decode_batches():
+    """Layer steps of at most 512 tokens go through bm_layer_step's single launch;
+    their kernel list is that one launch, their metric still the five ops' bytes."""
+    from baremetalinferenceengine_b200 import layer
+
+    dec = WORKLOADS["llama8b_decode_bf16"]
+    assert dec.fused and WORKLOADS["tinyllama_fp32"].fused
+    assert not WORKLOADS["llama70b_bf16"].fused and not WORKLOADS["swiglu_stress_bf16"].fused
+    assert [k for k, _ in dec.step_kernels()] == ["layer_step"]
+    b = dec.bytes_per_row()
+    assert dec.step_bytes() == (b["embed_gather"] + 2 * b["add_rmsnorm"] + b["rope_kv_store"] + b["swiglu"]) * 64
+    assert dec.step_kernels()[0][1] < dec.step_bytes()  # the single launch moves fewer bytes
+    assert layer.FUSED_MAX_ROWS == 512
+    big = WORKLOADS["llama70b_bf16"]
+    assert sum(n for _, n in big.step_kernels()) == big.step_bytes()

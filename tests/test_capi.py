@@ -209,3 +209,26 @@ def test_dropin_harness_links_against_this_library():
     und = subprocess.run(["nm", "-u", orc.REF_HARNESS_DROPIN], capture_output=True, text=True).stdout
     for mangled in LEGACY.values():
         assert mangled in und  # resolved from libbm_layer_ops.so, not the reference's kernels
+
+
+def test_layer_step_struct_layout_matches_the_header():
+    """The ctypes mirror of bm_layer_step_t has the C struct's size and field
+    offsets (gcc compiles the header and prints them)."""
+    fields = [name for name, _ in _lib.LayerStepC._fields_]
+    src = '#include <stddef.h>\n#include <stdio.h>\n#include "bm_layer_ops.h"\nint main(void) {\n'
+    src += '  printf("%zu\\n", sizeof(bm_layer_step_t));\n'
+    for f in fields:
+        src += f'  printf("%zu\\n", offsetof(bm_layer_step_t, {f}));\n'
+    src += "  return 0;\n}\n"
+    with tempfile.TemporaryDirectory() as tmp:
+        c, exe = os.path.join(tmp, "layout.c"), os.path.join(tmp, "layout")
+        with open(c, "w") as fh:
+            fh.write(src)
+        inc = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+        proc = subprocess.run(["gcc", "-std=c11", "-I", inc, "-I/usr/local/cuda/include", "-o", exe, c],
+                              capture_output=True, text=True)
+        assert proc.returncode == 0, proc.stderr
+        out = [int(x) for x in subprocess.run([exe], capture_output=True, text=True).stdout.split()]
+    assert out[0] == ctypes.sizeof(_lib.LayerStepC)
+    for f, off in zip(fields, out[1:]):
+        assert getattr(_lib.LayerStepC, f).offset == off, f
