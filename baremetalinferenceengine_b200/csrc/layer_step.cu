@@ -18,7 +18,7 @@
 //                  (a bad id keeps hidden's old row as h0, as the gather leaves it);
 //   token job t:   RoPE on q[t] and k[t], rotated k and raw v into the cache (the
 //                  block-per-token body of rope_kv.cu);
-//   SwiGLU job j:  1024 16-byte vectors of gate/up, 4 per thread.
+//   SwiGLU job j:  4 16-byte vectors of gate/up per thread.
 // No job waits for another. The results equal the five launches': h1 and h2 are
 // rounded to the storage type exactly where the separate kernels store them, the
 // residual and the copies are bit-identical, and the norms use the same formula
@@ -33,8 +33,11 @@
 namespace bm {
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
+// Blocks of 128 threads (each thread holding up to 8 of a row's 16-byte vectors)
+// for rows of at most 1024 vectors, 256 above: small blocks keep a decode batch's
+// jobs in one wave of resident blocks.
+constexpr int kMaxWarps = 8;
+constexpr int kMaxKV = 8;
 constexpr int kSwigluUnroll = 4;  // 16-byte vectors per operand per thread of a SwiGLU job
 #ifndef BM_STEP_FUSED_MAX_ROWS
 #define BM_STEP_FUSED_MAX_ROWS 512  // batches up to this many tokens take the single launch
@@ -65,29 +68,35 @@ struct StepArgs {
   int32_t* status;
 };
 
-// Block-wide sum; every thread gets it. `part` holds one slot per warp.
+// Block-wide sum over THREADS threads; every thread gets it. `part` holds one
+// slot per warp.
+template <int THREADS>
 __device__ __forceinline__ float block_sum(float v, float* part) {
   v = warp_sum(v);
   if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = v;
   __syncthreads();
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < kWarps; ++i) s += part[i];
+  for (int i = 0; i < THREADS / 32; ++i) s += part[i];
   return s;
 }
 
-template <typename T, int KV>
-__device__ __forceinline__ void row_job(const StepArgs& a, int64_t row, int tid, float (*part)[kWarps]) {
+template <typename T, int KV, int THREADS>
+__device__ __forceinline__ void row_job(const StepArgs& a, int64_t row, int tid, float (*part)[kMaxWarps]) {
   constexpr int N = VecWidth<T>::value;
+  // Narrow rows also hold the attention norm's weights from the start, so no load
+  // waits behind the first reduction (wider rows read them after it, from L2).
+  constexpr bool kEarlyWeights = KV <= 4;
   const int nv = a.dim / N;
   const int64_t off = row * a.dim;
-  uint4 e[KV], p1[KV], p2[KV];
+  uint4 e[KV], p1[KV], p2[KV], wa[kEarlyWeights ? KV : 1];
 #pragma unroll
   for (int k = 0; k < KV; ++k) {  // the deltas first: they do not wait for the id
-    const int v = tid + k * kThreads;
+    const int v = tid + k * THREADS;
     if (v < nv) {
       p1[k] = ld_stream(static_cast<const T*>(a.attn_out) + off + static_cast<int64_t>(v) * N);
       p2[k] = ld_stream(static_cast<const T*>(a.ffn_out) + off + static_cast<int64_t>(v) * N);
+      if constexpr (kEarlyWeights) wa[k] = ld_keep(static_cast<const T*>(a.w_attn) + static_cast<int64_t>(v) * N);
     }
   }
   const int32_t id = a.ids[row];
@@ -97,14 +106,14 @@ __device__ __forceinline__ void row_job(const StepArgs& a, int64_t row, int tid,
     const T* src = static_cast<const T*>(a.hidden) + off;  // the gather leaves the row as it was
 #pragma unroll
     for (int k = 0; k < KV; ++k) {
-      const int v = tid + k * kThreads;
+      const int v = tid + k * THREADS;
       if (v < nv) e[k] = ld_stream(src + static_cast<int64_t>(v) * N);
     }
   } else {
     const T* src = static_cast<const T*>(a.embed) + static_cast<int64_t>(id) * a.dim;
 #pragma unroll
     for (int k = 0; k < KV; ++k) {
-      const int v = tid + k * kThreads;
+      const int v = tid + k * THREADS;
       if (v < nv) e[k] = ld_keep(src + static_cast<int64_t>(v) * N);
     }
   }
@@ -112,7 +121,7 @@ __device__ __forceinline__ void row_job(const StepArgs& a, int64_t row, int tid,
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < KV; ++k) {
-    const int v = tid + k * kThreads;
+    const int v = tid + k * THREADS;
     if (v < nv) {
       float x[N], d[N];
       unpack16<T>(e[k], x);
@@ -124,14 +133,18 @@ __device__ __forceinline__ void row_job(const StepArgs& a, int64_t row, int tid,
       }
     }
   }
-  const float scale1 = rsqrtf(block_sum(ss, part[0]) / static_cast<float>(a.dim) + a.eps);
+  const float scale1 = rsqrtf(block_sum<THREADS>(ss, part[0]) / static_cast<float>(a.dim) + a.eps);
   ss = 0.f;
 #pragma unroll
   for (int k = 0; k < KV; ++k) {
-    const int v = tid + k * kThreads;
+    const int v = tid + k * THREADS;
     if (v < nv) {
       float w[N], y[N], d[N];
-      unpack16<T>(ld_keep(static_cast<const T*>(a.w_attn) + static_cast<int64_t>(v) * N), w);
+      if constexpr (kEarlyWeights) {
+        unpack16<T>(wa[k], w);
+      } else {
+        unpack16<T>(ld_keep(static_cast<const T*>(a.w_attn) + static_cast<int64_t>(v) * N), w);
+      }
 #pragma unroll
       for (int i = 0; i < N; ++i) y[i] = h[k][i] * scale1 * w[i];
       st_plain(static_cast<T*>(a.y_attn) + off + static_cast<int64_t>(v) * N, pack16<T>(y));
@@ -143,10 +156,10 @@ __device__ __forceinline__ void row_job(const StepArgs& a, int64_t row, int tid,
       }
     }
   }
-  const float scale2 = rsqrtf(block_sum(ss, part[1]) / static_cast<float>(a.dim) + a.eps);
+  const float scale2 = rsqrtf(block_sum<THREADS>(ss, part[1]) / static_cast<float>(a.dim) + a.eps);
 #pragma unroll
   for (int k = 0; k < KV; ++k) {
-    const int v = tid + k * kThreads;
+    const int v = tid + k * THREADS;
     if (v < nv) {
       float w[N], y[N];
       unpack16<T>(ld_keep(static_cast<const T*>(a.w_ffn) + static_cast<int64_t>(v) * N), w);
@@ -158,14 +171,14 @@ __device__ __forceinline__ void row_job(const StepArgs& a, int64_t row, int tid,
   }
 }
 
-template <typename T>
+template <typename T, int THREADS>
 __device__ __forceinline__ void swiglu_job(const StepArgs& a, int64_t job, int tid) {
   constexpr int N = VecWidth<T>::value;
-  const int64_t base = job * kThreads * kSwigluUnroll + tid;
+  const int64_t base = job * THREADS * kSwigluUnroll + tid;
   uint4 g[kSwigluUnroll], u[kSwigluUnroll];
 #pragma unroll
   for (int k = 0; k < kSwigluUnroll; ++k) {
-    const int64_t v = base + static_cast<int64_t>(k) * kThreads;
+    const int64_t v = base + static_cast<int64_t>(k) * THREADS;
     if (v < a.swiglu_nvec) {
       g[k] = ld_stream(static_cast<const T*>(a.gate) + v * N);
       u[k] = ld_stream(static_cast<const T*>(a.up) + v * N);
@@ -173,7 +186,7 @@ __device__ __forceinline__ void swiglu_job(const StepArgs& a, int64_t job, int t
   }
 #pragma unroll
   for (int k = 0; k < kSwigluUnroll; ++k) {
-    const int64_t v = base + static_cast<int64_t>(k) * kThreads;
+    const int64_t v = base + static_cast<int64_t>(k) * THREADS;
     if (v < a.swiglu_nvec) {
       float fg[N], fu[N];
       unpack16<T>(g[k], fg);
@@ -184,7 +197,7 @@ __device__ __forceinline__ void swiglu_job(const StepArgs& a, int64_t job, int t
     }
   }
   if (job == a.swiglu_jobs - 1) {  // elements past the last whole vector
-    for (int64_t i = a.swiglu_nvec * N + tid; i < a.swiglu_n; i += kThreads) {
+    for (int64_t i = a.swiglu_nvec * N + tid; i < a.swiglu_n; i += THREADS) {
       store1<T>(static_cast<T*>(a.act) + i,
                 swiglu1<T>(load1<T>(static_cast<const T*>(a.gate) + i), load1<T>(static_cast<const T*>(a.up) + i)));
     }
@@ -192,23 +205,26 @@ __device__ __forceinline__ void swiglu_job(const StepArgs& a, int64_t job, int t
 }
 
 // Blocks [0, rows): row jobs; [rows, rows + rope_jobs): token jobs; the rest: SwiGLU jobs.
-template <typename T, int KV>
-__global__ void __launch_bounds__(kThreads) layer_step_small_kernel(StepArgs a) {
+template <typename T, int KV, int THREADS>
+__global__ void __launch_bounds__(THREADS) layer_step_small_kernel(StepArgs a) {
   constexpr int N = VecWidth<T>::value;
   __shared__ float2 cs[ropekv::kMaxHalf];
-  __shared__ float part[2][kWarps];
+  __shared__ float part[2][kMaxWarps];
   const int tid = threadIdx.x;
   const int64_t job = blockIdx.x;
   const int64_t es = sizeof(T);
-  // the job's first lines, while the previous kernel finishes
+  // the job's first lines, while the previous kernel finishes (the norm weights,
+  // read by every row job, come into L2 for the later phases)
   if (job < a.rows) {
     if (tid == 0) prefetch_l2(a.ids + job);
-    prefetch_l2_range(static_cast<const T*>(a.attn_out) + job * a.dim, a.dim * es, tid, kThreads);
-    prefetch_l2_range(static_cast<const T*>(a.ffn_out) + job * a.dim, a.dim * es, tid, kThreads);
+    prefetch_l2_range(static_cast<const T*>(a.attn_out) + job * a.dim, a.dim * es, tid, THREADS);
+    prefetch_l2_range(static_cast<const T*>(a.ffn_out) + job * a.dim, a.dim * es, tid, THREADS);
+    prefetch_l2_range(a.w_attn, a.dim * es, tid, THREADS);
+    prefetch_l2_range(a.w_ffn, a.dim * es, tid, THREADS);
   } else if (job < a.rows + a.rope_jobs) {
-    ropekv::prefetch_token<T, ropekv::kFused>(a.rope, job - a.rows, tid, kThreads);
+    ropekv::prefetch_token<T, ropekv::kFused>(a.rope, job - a.rows, tid, THREADS);
   } else {
-    const int64_t v = (job - a.rows - a.rope_jobs) * kThreads * kSwigluUnroll + tid;
+    const int64_t v = (job - a.rows - a.rope_jobs) * THREADS * kSwigluUnroll + tid;
     if (v < a.swiglu_nvec) {
       prefetch_l2(static_cast<const T*>(a.gate) + v * N);
       prefetch_l2(static_cast<const T*>(a.up) + v * N);
@@ -216,25 +232,30 @@ __global__ void __launch_bounds__(kThreads) layer_step_small_kernel(StepArgs a) 
   }
   grid_dependency_wait();
   if (job < a.rows) {
-    row_job<T, KV>(a, job, tid, part);
+    row_job<T, KV, THREADS>(a, job, tid, part);
   } else if (job < a.rows + a.rope_jobs) {
-    ropekv::rope_kv_token<T, N, ropekv::kFused>(a.rope, job - a.rows, tid, kThreads, cs);
+    ropekv::rope_kv_token<T, N, ropekv::kFused>(a.rope, job - a.rows, tid, THREADS, cs);
   } else {
-    swiglu_job<T>(a, job - a.rows - a.rope_jobs, tid);
+    swiglu_job<T, THREADS>(a, job - a.rows - a.rope_jobs, tid);
   }
 }
+
+// Threads per block for rows of nv 16-byte vectors (at most kMaxKV per thread).
+int block_threads(int nv) { return nv <= kMaxKV * 128 ? 128 : 256; }
 
 template <typename T>
 int launch_small(const StepArgs& a, cudaStream_t stream) {
   constexpr int N = VecWidth<T>::value;
   const int nv = a.dim / N;
+  const int threads = block_threads(nv);
   const int64_t blocks = a.rows + a.rope_jobs + a.swiglu_jobs;
-  const dim3 grid(static_cast<unsigned>(blocks)), block(kThreads);
+  const dim3 grid(static_cast<unsigned>(blocks)), block(threads);
   const char* name = "layer_step_small_kernel";
-  if (nv <= kThreads) return launch_kernel(name, layer_step_small_kernel<T, 1>, grid, block, 0, stream, nullptr, a);
-  if (nv <= 2 * kThreads) return launch_kernel(name, layer_step_small_kernel<T, 2>, grid, block, 0, stream, nullptr, a);
-  if (nv <= 4 * kThreads) return launch_kernel(name, layer_step_small_kernel<T, 4>, grid, block, 0, stream, nullptr, a);
-  return launch_kernel(name, layer_step_small_kernel<T, 8>, grid, block, 0, stream, nullptr, a);
+  if (threads == 256) return launch_kernel(name, layer_step_small_kernel<T, 8, 256>, grid, block, 0, stream, nullptr, a);
+  if (nv <= 128) return launch_kernel(name, layer_step_small_kernel<T, 1, 128>, grid, block, 0, stream, nullptr, a);
+  if (nv <= 256) return launch_kernel(name, layer_step_small_kernel<T, 2, 128>, grid, block, 0, stream, nullptr, a);
+  if (nv <= 512) return launch_kernel(name, layer_step_small_kernel<T, 4, 128>, grid, block, 0, stream, nullptr, a);
+  return launch_kernel(name, layer_step_small_kernel<T, 8, 128>, grid, block, 0, stream, nullptr, a);
 }
 
 bool all_aligned16(std::initializer_list<const void*> ptrs) {
@@ -266,7 +287,7 @@ extern "C" int bm_layer_step(const bm_layer_step_t* s, bm_dtype_t dtype, int32_t
   const int es = dtype_size(dtype);
   const int vec = 16 / es;
   const int64_t n_ffn = s->rows * static_cast<int64_t>(s->ffn);
-  const bool small = s->rows <= kFusedMaxRows && s->dim % vec == 0 && s->dim / vec <= 8 * kThreads &&
+  const bool small = s->rows <= kFusedMaxRows && s->dim % vec == 0 && s->dim / vec <= kMaxKV * 256 &&
                      (s->head_dim / 2) % vec == 0 && s->head_dim / 2 <= ropekv::kMaxHalf &&
                      all_aligned16({s->embed, s->hidden, s->attn_out, s->w_attn, s->y_attn, s->ffn_out, s->w_ffn,
                                     s->y_ffn, s->gate, s->up, s->act}) &&
@@ -319,7 +340,8 @@ extern "C" int bm_layer_step(const bm_layer_step_t* s, bm_dtype_t dtype, int32_t
   a.act = s->act;
   a.swiglu_n = n_ffn;
   a.swiglu_nvec = n_ffn / vec;
-  a.swiglu_jobs = std::max<int64_t>(1, (a.swiglu_nvec + kThreads * kSwigluUnroll - 1) / (kThreads * kSwigluUnroll));
+  const int64_t per_job = static_cast<int64_t>(block_threads(s->dim / vec)) * kSwigluUnroll;
+  a.swiglu_jobs = std::max<int64_t>(1, (a.swiglu_nvec + per_job - 1) / per_job);
   a.status = d_status;
   ropekv::RopeArgs& r = a.rope;
   r.q = s->q;
