@@ -108,6 +108,37 @@ def test_head_dim_128_tile_edges_and_stale_cache(cuda, dt, hq, hkv, workspace):
     assert orc.worst_error(to_np(out), want) <= TOL[dt]
 
 
+@pytest.mark.parametrize("max_seq,lens", [
+    (8192, [8192]),             # one 8192-position sequence: 16 splits per (query, kv head)
+    (8192, [8192, 300]),        # a second, short query: its splits past 300 positions are empty
+    (1024, [1024, 1, 700]),     # 2 splits per query
+    (32768, [32768, 20000]),    # 64 splits per (query, kv head)
+])
+@pytest.mark.parametrize("workspace", [True, False], ids=["ws", "no_ws"])
+def test_tensor_core_few_pairs_long_sequences(cuda, max_seq, lens, workspace):
+    """bf16 head_dim 128 with fewer (query, kv head) pairs than the balanced kernel
+    takes: the per-pair grid splits each sequence (up to 64 splits, merged through
+    the workspace) or, without a workspace, runs each pair whole. Stale NaN past
+    each length stays out."""
+    batch, hq, hkv, hd = len(lens), 32, 8, 128
+    g = gen(max_seq + batch)
+    q = randn((batch, hq, hd), torch.bfloat16, g)
+    kc = randn((batch, hkv, max_seq, hd), torch.bfloat16, g)
+    vc = randn((batch, hkv, max_seq, hd), torch.bfloat16, g)
+    lens = torch.tensor(lens, dtype=torch.int32)
+    for b in range(batch):
+        kc[b, :, int(lens[b]):, :] = float("nan")
+        vc[b, :, int(lens[b]):, :] = float("nan")
+    seq_ids = torch.arange(batch, dtype=torch.int32)
+    status = ops.DeviceStatus(cuda)
+    out, _ = run(cuda, q, kc, vc, seq_ids, lens, workspace, status=status)
+    assert status.read() == 0
+    want, bad = oracle_attention(q, kc, vc, seq_ids, lens)
+    assert bad == 0
+    assert torch.isfinite(out.float()).all()
+    assert orc.worst_error(to_np(out), want) <= TOL[torch.bfloat16]
+
+
 @pytest.mark.parametrize("dt", ORACLE_DT, ids=["f32", "bf16"])
 def test_stale_workspace_contents_do_not_leak(cuda, dt):
     """Splits that lie past a query's length write only their (max, sum); the

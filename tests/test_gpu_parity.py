@@ -353,6 +353,48 @@ def test_rope_kv_store_large_batches(cuda, use_table, dt, rows, hq, hkv, hd):
 
 
 @pytest.mark.parametrize("dt", DTYPES, ids=["f32", "bf16"])
+@pytest.mark.parametrize("table_len,hd", [(1000, 128), (8192, 128), (256, 48), (3, 64)])
+def test_rope_on_chip_table_boundaries(cuda, dt, table_len, hd):
+    """Batches of >= 512 tokens with a table take (cos, sin) from the on-chip table:
+    fine rows 0..L-1 and coarse rows 0, L, 2L, ... in shared memory, combined by angle
+    addition. Positions on both sides of every L boundary, the last table row, and
+    position 0, for a table length that is not a power of two as well: within the
+    tolerance of the double-precision oracle, and position 0 exactly the identity."""
+    rows, hq, hkv = 1024, 8, 2
+    g = gen(table_len + hd)
+    lg = min(range(0, 31), key=lambda e: (-(-table_len // 2**e) + 2**e) if 2**e <= table_len else 1 << 40)
+    L = 2 ** lg
+    edge = sorted({p for b in range(0, table_len, L) for p in (b - 1, b, b + 1) if 0 <= p < table_len}
+                  | {0, table_len - 1})
+    pos = torch.tensor((edge * (rows // len(edge) + 1))[:rows], dtype=torch.int32)
+    pos[:8] = 0
+    q, k = randn((rows, hq, hd), dt, g), randn((rows, hkv, hd), dt, g)
+    table = ops.RopeTable(table_len, hd, 5e5, cuda)
+    qd, kd = q.to(cuda), k.to(cuda)
+    status = ops.DeviceStatus(cuda)
+    ops.rope(qd, kd, pos.to(cuda), table=table, status=status)
+    assert status.read() == 0
+    assert worst(qd, orc.rope(to_np(q), pos.numpy(), 5e5)) <= TOL[dt]
+    assert worst(kd, orc.rope(to_np(k), pos.numpy(), 5e5)) <= TOL[dt]
+    assert bits_equal(qd[:8], q[:8])  # position 0: the identity, bit for bit
+    # the fused form (K into the cache): the edge positions repeated, each repetition
+    # in its own sequence, so every (sequence, position) slot is written once
+    fpos = torch.tensor((edge * (rows // len(edge) + 1))[:rows], dtype=torch.int32)
+    seq = torch.arange(rows, dtype=torch.int32) // len(edge)
+    v = randn((rows, hkv, hd), dt, g)
+    kc = torch.zeros(int(seq.max()) + 1, hkv, table_len, hd, dtype=dt)
+    qd, kcd, vcd = q.to(cuda), kc.to(cuda), kc.clone().to(cuda)
+    ops.rope_kv_store(qd, k.to(cuda), v.to(cuda), fpos.to(cuda), kcd, vcd, table=table, seq_ids=seq.to(cuda),
+                      status=status)
+    assert status.read() == 0
+    want_q, want_kc, _, bad = orc.rope_kv_store(to_np(q), to_np(k), to_np(v), fpos.numpy(), to_np(kc), to_np(kc),
+                                                5e5, seq_ids=seq.numpy())
+    assert bad == 0
+    assert worst(qd, want_q) <= TOL[dt]
+    assert worst(kcd, want_kc) <= TOL[dt]
+
+
+@pytest.mark.parametrize("dt", DTYPES, ids=["f32", "bf16"])
 @pytest.mark.parametrize("hq,hkv,hd", [(6, 6, 48), (6, 3, 48), (8, 8, 128), (5, 1, 6), (4, 2, 34)])
 def test_rope_in_place(cuda, dt, hq, hkv, hd):
     """Batched launch_rope, incl. the reference's GQA-shaped case (6/3 heads) and
