@@ -297,6 +297,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // faster than 8 on the 70B FFN (16384 x 8192 -> 28672) and no slower on the 8B one
 #define BM_GEMM_PAIR_GROUP_M 16
 #endif
+#ifndef BM_GEMM_WIDE_SWIGLU
+#define BM_GEMM_WIDE_SWIGLU 1  // bm_gemm_swiglu over more than one row block: the wide tile below
+#endif
 constexpr int kPairStages = BM_GEMM_PAIR_STAGES;
 constexpr int kPairStageBytes = kABytes + kBBytes / 2;           // 16 KB of A + 16 KB of B: 32 KB
 constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 1024 + 256;
@@ -505,6 +508,201 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
 }
 
+// Wide SwiGLU tiles for CTA pairs: each pair computes 256 rows x 256 outputs with
+// two MMAs per K slice (M=256, N=256: gate, then up) that share the A slice, so
+// every SM reads 48 KB of operands per 256 cycles of math where the tile above
+// reads 32 KB per 128 (a quarter fewer L2 -> shared-memory bytes per FLOP; the
+// tile above waits on arriving operands about 40 % of the time). Each CTA loads
+// its 128 rows of A and its half (128 columns) of both weights' 256; the two
+// accumulators fill all 512 TMEM columns, so a tile's MMAs wait for the previous
+// tile's epilogue, which eight warps (two per TMEM lane quarter, one per column
+// half) drain. Four stages of 48 KB.
+constexpr int kWideStages = 4;
+constexpr int kWideHalfB = kBBoxBytes * 2;                        // 128 weight columns x 64 K: 16 KB
+constexpr int kWideStageBytes = kABytes + 2 * kWideHalfB;         // 48 KB
+constexpr int kWideSmemBytes = kWideStages * kWideStageBytes + 1024 + 256;
+static_assert(kWideSmemBytes <= 232448, "shared memory per CTA");
+constexpr int kWideOut = 256;                                     // output columns per tile
+constexpr int kWideEpilogueThreads = 256;
+constexpr int kWideThreads = 64 + kWideEpilogueThreads;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWideThreads, 1)
+    gemm_tc_wide_swiglu_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tg,
+                               const __grid_constant__ CUtensorMap tu, const Args a) {
+  grid_dependency_wait();
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                         ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kWideStages * kWideStageBytes);
+  uint64_t* empty = full + kWideStages;
+  uint64_t* acc_full = empty + kWideStages;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* mma_done = acc_empty + 1;
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_s + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0: the leader, which issues the MMAs
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int tiles = a.m_blocks * a.n_blocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kWideStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 2 * kWideEpilogueThreads);
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_base_s, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any copy or arrival reaches them
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_s;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t last_parity[kWideStages];
+    bool filled[kWideStages];
+    for (int s = 0; s < kWideStages; ++s) filled[s] = false;
+    bool ok = true;
+    for (int t = pair; t < tiles && ok; t += npairs) {
+      int mb, nb;
+      pair_tile_coords(a, t, &mb, &nb);
+      const int m0 = mb * 2 * kBlockM + static_cast<int>(rank) * kBlockM;
+      const int nh = nb * kWideOut + static_cast<int>(rank) * (kWideOut / 2);  // this CTA's half of the columns
+      for (int ks = 0; ks < a.k_steps; ++ks) {
+        if (!wait_phase(&empty[stage], phase ^ 1u, abort_flag, a.status, kWaitLimitNs, true)) {
+          ok = false;
+          break;
+        }
+        unsigned char* sa = smem + stage * kWideStageBytes;
+        unsigned char* sg = sa + kABytes;
+        unsigned char* su = sg + kWideHalfB;
+        const uint32_t bar = cluster_addr(&full[stage], 0);
+        if (leader) mbar_expect_tx(&full[stage], 2 * kWideStageBytes);
+        const int k0 = ks * kBlockK;
+        tma_load_2d_pair(sa, &ta, bar, k0, m0);
+        tma_load_2d_pair(sg, &tg, bar, nh, k0);
+        tma_load_2d_pair(sg + kBBoxBytes, &tg, bar, nh + kBoxN, k0);
+        tma_load_2d_pair(su, &tu, bar, nh, k0);
+        tma_load_2d_pair(su + kBBoxBytes, &tu, bar, nh + kBoxN, k0);
+        filled[stage] = true;
+        last_parity[stage] = phase;
+        if (++stage == kWideStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (leader) {  // every copy of the pair counts on the leader's barriers: let them land
+      for (int s = 0; s < kWideStages; ++s) {
+        if (filled[s]) wait_phase(&full[s], last_parity[s], abort_flag, a.status, kDrainLimitNs, false);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer (leader) ----------------
+    bool issued = false;
+    if (leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += npairs) {
+        if (!wait_phase(acc_empty, acc_phase ^ 1u, abort_flag, a.status, kWaitLimitNs, true)) break;
+        tc_fence_after();
+        for (int ks = 0; ks < a.k_steps; ++ks) {
+          if (!wait_phase(&full[stage], phase, abort_flag, a.status, kWaitLimitNs, true)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * kWideStageBytes);
+          const uint32_t sg = sa + kABytes;
+          const uint32_t su = sg + kWideHalfB;
+#pragma unroll
+          for (int kk = 0; kk < kBlockK / 16; ++kk) {
+            const uint64_t a_desc = smem_desc(sa + kk * 32, 16, 1024);
+            const uint32_t acc = (ks | kk) != 0 ? 1u : 0u;
+            mma_bf16_pair(tmem_base, a_desc, smem_desc(sg + kk * 2048, kBBoxBytes, 1024), kPairInstrDesc, acc);
+            mma_bf16_pair(tmem_base + kWideOut, a_desc, smem_desc(su + kk * 2048, kBBoxBytes, 1024),
+                          kPairInstrDesc, acc);
+          }
+          issued = true;
+          mma_commit_pair(&empty[stage], 0x3);  // both CTAs may refill this stage
+          if (++stage == kWideStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair(acc_full, 0x3);
+        acc_phase ^= 1u;
+      }
+      // no pair MMA may still write either CTA's TMEM when it is freed: the leader
+      // drains them here, and the cluster barrier at the end holds the peer back
+      if (issued) {
+        mma_commit_pair(mma_done, 0x3);
+        wait_phase(mma_done, 0, abort_flag, a.status, kDrainLimitNs, false);
+      }
+    }
+  } else if (warp >= 2) {
+    // ---------------- epilogue (both CTAs, eight warps) ----------------
+    const int quarter = warp & 3;             // the TMEM lanes this warp may read
+    const int half = (warp - 2) >> 2;         // which 128 of the tile's 256 output columns
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    uint32_t acc_phase = 0;
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
+    for (int t = pair; t < tiles; t += npairs) {
+      int ok = 1;
+      if (lane == 0) ok = wait_phase(acc_full, acc_phase, abort_flag, a.status, kWaitLimitNs, true);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      int mb, nb;
+      pair_tile_coords(a, t, &mb, &nb);
+      const int64_t row = static_cast<int64_t>(mb) * 2 * kBlockM + rank * kBlockM + quarter * 32 + lane;
+      const uint32_t tbase = tmem_base + lane_addr;
+      const int n0 = nb * kWideOut;
+#pragma unroll 1
+      for (int c = half * (kWideOut / 2); c < (half + 1) * (kWideOut / 2); c += 32) {
+        uint32_t g[32], u[32];
+        float o[32];
+        tmem_load32(tbase + c, g);
+        tmem_load32(tbase + kWideOut + c, u);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = silu(__uint_as_float(g[i])) * __uint_as_float(u[i]);
+        if (row < a.rows) {
+          __nv_bfloat16* dst = out + row * a.n + n0 + c;
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            if (n0 + c + v * 8 < a.n) st_plain(dst + v * 8, pack16<__nv_bfloat16>(o + v * 8));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(cluster_addr(acc_empty, 0));
+      acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA leaves while the other may still reach its shared memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 
@@ -540,12 +738,20 @@ int run(const char* what, void* out, const void* x, const void* w0, const void* 
   const bool paired = rows > kBlockM && sm_count() >= 2;
   const int block_rows = paired ? 2 * kBlockM : kBlockM;
   a.m_blocks = static_cast<int>((rows + block_rows - 1) / block_rows);
-  const int out_cols = SWIGLU ? kBlockN / 2 : kBlockN;
+  const bool wide = SWIGLU && paired && BM_GEMM_WIDE_SWIGLU;
+  const int out_cols = wide ? kWideOut : SWIGLU ? kBlockN / 2 : kBlockN;
   a.n_blocks = (n + out_cols - 1) / out_cols;
   a.k_steps = (k + kBlockK - 1) / kBlockK;
   a.status = d_status;
   const int64_t tiles = static_cast<int64_t>(a.m_blocks) * a.n_blocks;
   if (tiles > (int64_t{1} << 31) - 1) return fail(BM_ERR_INVALID_ARGUMENT, "%s: too many tiles", what);
+  if (wide) {
+    const int grid = 2 * static_cast<int>(std::min<int64_t>(tiles, sm_count() / 2));
+    auto kernel = gemm_tc_wide_swiglu_kernel;
+    if (int st = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), kWideSmemBytes, what)) return st;
+    return launch_kernel(what, kernel, dim3(grid), dim3(kWideThreads), kWideSmemBytes, as_stream(stream), nullptr,
+                         ta, tb0, tb1, a);
+  }
   if (paired) {
     const int grid = 2 * static_cast<int>(std::min<int64_t>(tiles, sm_count() / 2));
     auto kernel = gemm_tc_pair_kernel<SWIGLU>;
