@@ -40,6 +40,8 @@ ATTENTION_SHAPES = {
     "70b_decode_b64_full": (64, 64, 8, 128, 8192, "full", torch.bfloat16),
     "70b_decode_b16_ragged": (16, 64, 8, 128, 8192, "uniform", torch.bfloat16),
     "8b_single_sequence": (1, 32, 8, 128, 8192, "full", torch.bfloat16),
+    "8b_decode_b2_full": (2, 32, 8, 128, 8192, "full", torch.bfloat16),
+    "70b_decode_b2_ragged": (2, 64, 8, 128, 8192, "uniform", torch.bfloat16),
     "8b_decode_b64_full_fp32": (64, 32, 8, 128, 8192, "full", torch.float32),
 }
 # name: (rows, dim, hidden)
