@@ -142,7 +142,8 @@ class LayerBuffers:
     """Device buffers of one layer step, seeded N(0,1) activations, 1+N(0,0.02)
     norm weights, N(0,0.02) embedding table, uniform token ids."""
 
-    def __init__(self, shape: LayerShape, device, seed: int = 0, row_offset: int = 0, with_table: bool = True):
+    def __init__(self, shape: LayerShape, device, seed: int = 0, row_offset: int = 0, with_table: bool = True,
+                 packed: bool = False):
         s = shape
         self.shape = s
         self.device = torch.device(device)
@@ -197,6 +198,55 @@ class LayerBuffers:
         self.act = torch.empty(R, s.ffn, dtype=dt, device=self.device)
         self.table = ops.RopeTable(s.max_seq, s.hd, s.theta, self.device) if with_table else None
         self.status = ops.DeviceStatus(self.device)
+        self.arena = None
+        if packed:
+            self._pack()
+
+    # Arena order: tensors only read, then those read and written, then those only
+    # written, each at a 256-byte boundary; so a step's inputs are one contiguous
+    # range ([0, in_end)) and its outputs another ([out_start, end)).
+    def _arena_groups(self):
+        ins, out = self.inputs(), self.outputs()
+        both = tuple(n for n in ins if n in out)
+        return tuple(n for n in ins if n not in both), both, tuple(n for n in out if n not in both)
+
+    def _pack(self) -> None:
+        """Moves the step's inputs and outputs into one device allocation (views at
+        256-byte boundaries), so a host-buffer step copies in one range and back
+        one range."""
+        only_in, both, only_out = self._arena_groups()
+        offsets, off = {}, 0
+        for n in only_in + both + only_out:
+            t = getattr(self, n)
+            offsets[n] = off
+            off += -(-t.numel() * t.element_size() // 256) * 256
+        arena = torch.empty(off, dtype=torch.uint8, device=self.device)
+        self.arena_offsets = offsets
+        for n, o in offsets.items():
+            t = getattr(self, n)
+            view = arena[o:o + t.numel() * t.element_size()].view(t.dtype).view(t.shape)
+            view.copy_(t)
+            setattr(self, n, view)
+        self.arena = arena
+        last_in = (only_in + both)[-1]
+        self.in_end = offsets[last_in] + getattr(self, last_in).numel() * getattr(self, last_in).element_size()
+        self.out_start = offsets[(both + only_out)[0]]
+
+    def with_arena(self, arena: torch.Tensor) -> "LayerBuffers":
+        """A shallow copy whose step inputs and outputs are views into `arena` (same
+        size and layout as self.arena); everything else (the table, weights, caches,
+        status word) is shared. Two arenas let one step's outputs go back while the
+        next step's inputs come in."""
+        import copy
+
+        if self.arena is None or arena.numel() != self.arena.numel():
+            raise ValueError("with_arena needs a packed LayerBuffers and an arena of the same size")
+        other = copy.copy(self)
+        for n, o in self.arena_offsets.items():
+            t = getattr(self, n)
+            setattr(other, n, arena[o:o + t.numel() * t.element_size()].view(t.dtype).view(t.shape))
+        other.arena = arena
+        return other
 
     def inputs(self) -> tuple:
         """Tensors an end-to-end (host-buffer) step copies in, every step."""

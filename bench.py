@@ -665,7 +665,11 @@ def main() -> int:
     job_rows = shape.rows * (world if args.scaling == "weak" else 1)
     log(f"[rank {rank}] allocating {local.name}: tokens [{rows.start}, {rows.stop}) of {job_rows}, "
         f"{local.step_bytes() / 1e9:.2f} GB per step")
-    b = layer.LayerBuffers(local, dev, seed=1000 + rank, row_offset=rows.start)
+    # the same timing branch on every rank: decided by the largest rank's block
+    small = shape.with_rows(-(-job_rows // world)).step_bytes() < L2_RESIDENT_BYTES
+    # an L2-resident step keeps its inputs and outputs in one arena: its host-buffer
+    # (e2e) form is one copy in and one copy out
+    b = layer.LayerBuffers(local, dev, seed=1000 + rank, row_offset=rows.start, packed=small)
     stream = torch.cuda.Stream(dev)
     kernels = local.step_kernels()
     nk = len(kernels)
@@ -676,8 +680,6 @@ def main() -> int:
     stream.synchronize()
     assert b.status.read(stream) == 0, "device status set during warm-up"
 
-    # the same timing branch on every rank: decided by the largest rank's block
-    small = shape.with_rows(-(-job_rows // world)).step_bytes() < L2_RESIDENT_BYTES
     launches = 0
     if not small:
         # Inputs far larger than L2: K back-to-back steps, events between launches.
@@ -1072,17 +1074,51 @@ def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
     def pinned(t):
         return torch.empty((R,) + tuple(t.shape[1:]), dtype=t.dtype, device="cpu", pin_memory=True)
 
-    h_in = {n: pinned(getattr(b, n)) for n in names_in}
-    h_out = {n: pinned(getattr(b, n)) for n in names_out}
-    for n in names_in:
-        h_in[n].copy_(getattr(b, n)[:R])
     h2d, comp, d2h = (torch.cuda.Stream(dev) for _ in range(3))
     chunks = 1 if small else max(1, min(args.e2e_chunks, R))
     size = math.ceil(R / chunks)
     slices = [slice(i, min(R, i + size)) for i in range(0, R, size)]
     done = torch.cuda.Event()
+    arena = small and b.arena is not None and R == shape.rows
+    if arena:
+        # one copy in (every input, q included) and one copy out (q and every output),
+        # alternating between two arenas so a step's outputs go back while the next
+        # step's inputs come in
+        h_arena_in = torch.empty(b.in_end, dtype=torch.uint8, pin_memory=True)
+        h_arena_out = [torch.empty(b.arena.numel() - b.out_start, dtype=torch.uint8, pin_memory=True)
+                       for _ in range(2)]
+        h_arena_in.copy_(b.arena[:b.in_end])
+        bufs = [b, b.with_arena(torch.empty_like(b.arena))]
+        free = [torch.cuda.Event(), torch.cuda.Event()]
+        parity = [0]
+    else:
+        h_in = {n: pinned(getattr(b, n)) for n in names_in}
+        h_out = {n: pinned(getattr(b, n)) for n in names_out}
+        for n in names_in:
+            h_in[n].copy_(getattr(b, n)[:R])
+
+    def step_arena():
+        x = parity[0]
+        parity[0] ^= 1
+        bx = bufs[x]
+        h2d.wait_event(free[x])  # the step two back, on this arena, has been copied out
+        ev_in, ev_k = torch.cuda.Event(), torch.cuda.Event()
+        with torch.cuda.stream(h2d):
+            bx.arena[:b.in_end].copy_(h_arena_in, non_blocking=True)
+            ev_in.record(h2d)
+        comp.wait_event(ev_in)
+        with torch.cuda.stream(comp):
+            layer.run_step(bx, comp)
+            ev_k.record(comp)
+        d2h.wait_event(ev_k)
+        with torch.cuda.stream(d2h):
+            h_arena_out[x].copy_(bx.arena[b.out_start:], non_blocking=True)
+            free[x].record(d2h)
+        done.record(d2h)
 
     def step():
+        if arena:
+            return step_arena()
         h2d.wait_event(done)
         comp.wait_event(done)
         for sl in slices:
@@ -1118,11 +1154,15 @@ def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
     torch.cuda.synchronize(dev)
     barrier()
     ms = max_over_ranks([t0.elapsed_time(t1)])[0]
-    del h_in, h_out
+    if arena:
+        bin_, bout = b.in_end, b.arena.numel() - b.out_start
+        del h_arena_in, h_arena_out
+    else:
+        bin_, bout = bytes_per_row(b, names_in) * R, bytes_per_row(b, names_out) * R
+        del h_in, h_out
     link = pcie_link(dev, h2d, d2h, barrier, max_over_ranks, world)
     step_bytes = shape.with_rows(R).step_bytes()
     gbs = world * step_bytes * E / (ms / 1e3) / 1e9
-    bin_, bout = bytes_per_row(b, names_in) * R, bytes_per_row(b, names_out) * R
     h2d_rate = bin_ / (ms / E / 1e3) / 1e9
     # host-side lower bound of one step on this GPU while every GPU copies, then the job's
     t_link = max(bin_ / (link["h2d_gbs"] * 1e9), bout / (link["d2h_gbs"] * 1e9),
@@ -1137,9 +1177,11 @@ def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
                          "how": "max over GPUs of max(H2D bytes / H2D rate, D2H bytes / D2H rate, both / "
                                 "bidirectional rate), the rates measured with all GPUs copying at once"},
             "frac_of_link": round(gbs / roof, 3),
-            "how": "per step: pinned-host -> device copies of every input, the five kernels, device -> pinned-host "
-                   "copies of every output, chunked over rows on three streams; CUDA events, max over ranks; host "
-                   "buffers pinned after binding the rank to its GPU's NUMA-local CPUs"}
+            "copies": "one H2D copy of the step's input arena and one D2H copy of its output arena" if arena else
+                      f"one copy per tensor and chunk ({len(slices)} chunks over rows)",
+            "how": "per step: pinned-host -> device copies of every input, the step's kernels, device -> pinned-host "
+                   "copies of every output, on three streams (chunks overlap copies and kernels); CUDA events, max "
+                   "over ranks; host buffers pinned after binding the rank to its GPU's NUMA-local CPUs"}
 
 
 if __name__ == "__main__":
