@@ -80,3 +80,34 @@ def test_run_step_uses_one_launch_for_decode_batches():
     assert layer.FUSED_MAX_ROWS == 512
     big = WORKLOADS["llama70b_bf16"]
     assert sum(n for _, n in big.step_kernels()) == big.step_bytes()
+
+
+def test_packed_step_buffers_are_two_contiguous_ranges():
+    """A decode-sized step keeps its tensors in one arena: the inputs (q last) form
+    [0, in_end), the outputs (q first) [out_start, end), each tensor at a 256-byte
+    boundary, with the same seeded values as separate buffers; with_arena binds the
+    same step to a second arena and shares everything else."""
+    import torch
+
+    from baremetalinferenceengine_b200 import layer
+
+    for name in ("llama8b_decode_bf16", "tinyllama_fp32", "swiglu_stress_bf16"):
+        shape = WORKLOADS[name].with_rows(24)
+        b = layer.LayerBuffers(shape, "cpu", seed=5, with_table=False, packed=True)
+        plain = layer.LayerBuffers(shape, "cpu", seed=5, with_table=False)
+        base = b.arena.data_ptr()
+        spans = {}
+        for n in set(b.inputs()) | set(b.outputs()):
+            t = getattr(b, n)
+            off = t.data_ptr() - base
+            assert off % 256 == 0 and t.is_contiguous()
+            spans[n] = (off, off + t.numel() * t.element_size())
+        for n in b.inputs():
+            assert spans[n][1] <= b.in_end
+            assert torch.equal(getattr(b, n), getattr(plain, n))
+        for n in b.outputs():
+            assert spans[n][0] >= b.out_start and spans[n][1] <= b.arena.numel()
+        assert b.out_start <= b.in_end  # q (when the step has it) lies in both ranges
+        other = b.with_arena(torch.zeros_like(b.arena))
+        assert other.embed is b.embed and other.k_cache is b.k_cache and other.status is b.status
+        assert all(getattr(other, n).data_ptr() != getattr(b, n).data_ptr() for n in spans)
