@@ -133,6 +133,10 @@ int bm_swiglu(void* out, const void* gate, const void* up, int64_t n,
  *   bm_add_rmsnorm(hidden += ffn_out; y_ffn = rmsnorm(hidden) * w_ffn)
  *   bm_swiglu(act = silu(gate) * up)
  * No single reference function: it groups the reference's per-token calls.
+ * Every input (the GEMM and attention outputs included) must be ready when it is
+ * called; inside one transformer layer they are not (attn_out depends on y_attn
+ * through the projections and the attention), so a layer loop calls the ops
+ * separately and this one-call form serves steps whose inputs are at hand together.
  * Batches of at most 512 tokens with 16-byte aligned buffers and whole-vector
  * rows run as ONE launch (the only dependency between the ops is the row-local
  * residual, so the launch holds independent row, token and SwiGLU jobs); larger
