@@ -73,6 +73,8 @@ def test_gemm_matches_the_oracle(cuda, m, n, k):
     (129, 512, 384),      # one row past a row block
     (512, 2048, 2048),
     (8, 8, 8),            # the smallest legal shape
+    (257, 192, 384),      # wide tile: rows one past a pair block; the 2nd tile's upper column half past the end
+    (4097, 512, 288),     # wide tile: 17 pair row blocks (past a tile group of 16); a tile mostly past the columns
 ])
 def test_gemm_swiglu_matches_the_oracle(cuda, rows, dim, hidden):
     g = gen(rows * 5 + dim + hidden)
