@@ -12,10 +12,11 @@ Llama-3-70B shape: 131072 tokens (16 sequences x 8192 positions), dim 8192,
 64 Q / 8 KV heads of 128, FFN 28672, bf16 — 49 GB of algorithmic traffic per
 step, far above the 126 MB L2, so no flush is needed between steps.
 
-N > 1 runs one process per GPU (torchrun); every rank owns its own batch of
-tokens (weak scaling: the job grows with N, rows are independent, no
-collectives on the data path). Time is the max over ranks of the CUDA-event
-time of exactly K steps, bracketed by a barrier and a synchronize.
+N > 1 runs one process per GPU (torchrun); the workload's tokens are one job
+split into contiguous blocks of ceil(R/N), one per rank (strong scaling, the
+default; --scaling weak gives every rank its own copy of the batch). Rows are
+independent: no collectives on the data path. Time is the max over ranks of the
+CUDA-event time of exactly K steps, bracketed by a barrier and a synchronize.
 
 value: whole-job algorithmic HBM GB/s (bytes every kernel must move / time).
 e2e:   the same metric with the step's inputs copied in from pinned host memory
@@ -993,11 +994,15 @@ def ref_gpu_baseline(shape, dev, max_rows: int, our_rows_per_s: float) -> dict:
                       f"the default stream, median of 3"}
 
 
-def pcie_link(dev, h2d, d2h, barrier, max_over_ranks, world: int, nbytes: int = 1 << 30, reps: int = 3) -> dict:
+def pcie_link(dev, h2d, d2h, barrier, max_over_ranks, world: int, nbytes: int = 1 << 30, reps: int = 3,
+              mix=None) -> dict:
     """Host<->device bandwidth of pinned copies, the roofline of the e2e leg: H2D
     alone, D2H alone, and both directions at once on two streams. Every rank
     copies at the same time (a barrier before each phase), so the per-GPU rates
-    are those each GPU gets while all N copy: the host side is shared."""
+    are those each GPU gets while all N copy: the host side is shared.
+    mix = (h2d_bytes, d2h_bytes) of one step adds a fourth phase, both directions
+    at once in that ratio (the larger side nbytes): the time the link needs for
+    the step's own copies, with nothing else running."""
     import torch
 
     host_a = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
@@ -1028,13 +1033,24 @@ def pcie_link(dev, h2d, d2h, barrier, max_over_ranks, world: int, nbytes: int = 
     t_down, t_down_all = timed([(d2h, down)])
     t_both, t_both_all = timed([(h2d, up), (d2h, down)])
     gb = nbytes * reps / 1e9
+    out = {"h2d_gbs": round(gb / t_up, 1), "d2h_gbs": round(gb / t_down, 1),
+           "bidirectional_gbs": round(2 * gb / t_both, 1),
+           "aggregate": {"h2d_gbs": round(world * gb / t_up_all, 1), "d2h_gbs": round(world * gb / t_down_all, 1),
+                         "bidirectional_gbs": round(2 * world * gb / t_both_all, 1), "gpus": world},
+           "how": f"pinned 1 GiB copies x{reps} per GPU, all {world} GPU(s) at once, CUDA events; per-GPU rates "
+                  f"are this GPU's own, aggregate = all GPUs' bytes / the slowest GPU's time"}
+    if mix is not None and max(mix) > 0:
+        scale = nbytes / max(mix)
+        n_up, n_down = (min(nbytes, int(x * scale)) // 512 * 512 for x in mix)
+        up_mix = lambda: dev_a[:n_up].copy_(host_a[:n_up], non_blocking=True)  # noqa: E731
+        down_mix = lambda: host_b[:n_down].copy_(dev_b[:n_down], non_blocking=True)  # noqa: E731
+        _, t_mix_all = timed([(h2d, up_mix), (d2h, down_mix)])
+        # seconds the link needs for one step's copies (every GPU copying its own at once)
+        out["step_mix"] = {"h2d_bytes": n_up, "d2h_bytes": n_down, "s_per_step": t_mix_all / reps / scale,
+                           "how": "H2D and D2H at once in the step's byte ratio, all GPUs at once, scaled to "
+                                  "one step's bytes; the slowest GPU's time"}
     del host_a, host_b, dev_a, dev_b
-    return {"h2d_gbs": round(gb / t_up, 1), "d2h_gbs": round(gb / t_down, 1),
-            "bidirectional_gbs": round(2 * gb / t_both, 1),
-            "aggregate": {"h2d_gbs": round(world * gb / t_up_all, 1), "d2h_gbs": round(world * gb / t_down_all, 1),
-                          "bidirectional_gbs": round(2 * world * gb / t_both_all, 1), "gpus": world},
-            "how": f"pinned 1 GiB copies x{reps} per GPU, all {world} GPU(s) at once, CUDA events; per-GPU rates "
-                   f"are this GPU's own, aggregate = all GPUs' bytes / the slowest GPU's time"}
+    return out
 
 
 def bytes_per_row(b, names) -> float:
@@ -1044,7 +1060,8 @@ def bytes_per_row(b, names) -> float:
 def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
     """The same step through the public API with host buffers: every step copies
     its inputs in from pinned host memory and its outputs back, chunked over rows
-    so copies in both directions overlap the kernels of other chunks. Its
+    so copies in both directions overlap the kernels of other chunks, and the
+    next step's first chunks come in while this step's last chunks go out. Its
     roofline is the host link measured with every GPU copying at once: a step
     cannot end before its H2D bytes, its D2H bytes and their sum have crossed at
     the measured H2D, D2H and bidirectional rates."""
@@ -1078,7 +1095,6 @@ def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
     chunks = 1 if small else max(1, min(args.e2e_chunks, R))
     size = math.ceil(R / chunks)
     slices = [slice(i, min(R, i + size)) for i in range(0, R, size)]
-    done = torch.cuda.Event()
     arena = small and b.arena is not None and R == shape.rows
     if arena:
         # one copy in (every input, q included) and one copy out (q and every output),
@@ -1114,15 +1130,19 @@ def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
         with torch.cuda.stream(d2h):
             h_arena_out[x].copy_(bx.arena[b.out_start:], non_blocking=True)
             free[x].record(d2h)
-        done.record(d2h)
+
+    # chunk_out[j]: the last D2H of chunk j's rows. The next step's H2D into those
+    # rows waits for it (its inputs were consumed by then and q, an input updated
+    # in place, has been read back), so the next step's first chunks come in while
+    # this step's last chunks go out.
+    chunk_out = [torch.cuda.Event() for _ in slices]
 
     def step():
         if arena:
             return step_arena()
-        h2d.wait_event(done)
-        comp.wait_event(done)
-        for sl in slices:
+        for sl, out_ev in zip(slices, chunk_out):
             ev_in, ev_k = torch.cuda.Event(), torch.cuda.Event()
+            h2d.wait_event(out_ev)
             with torch.cuda.stream(h2d):
                 for n in names_in:
                     getattr(b, n)[sl].copy_(h_in[n][sl], non_blocking=True)
@@ -1135,7 +1155,7 @@ def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
             with torch.cuda.stream(d2h):
                 for n in names_out:
                     h_out[n][sl].copy_(getattr(b, n)[sl], non_blocking=True)
-        done.record(d2h)
+                out_ev.record(d2h)
 
     for _ in range(2):
         step()
@@ -1160,13 +1180,15 @@ def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
     else:
         bin_, bout = bytes_per_row(b, names_in) * R, bytes_per_row(b, names_out) * R
         del h_in, h_out
-    link = pcie_link(dev, h2d, d2h, barrier, max_over_ranks, world)
+    link = pcie_link(dev, h2d, d2h, barrier, max_over_ranks, world, mix=(bin_, bout))
     step_bytes = shape.with_rows(R).step_bytes()
     gbs = world * step_bytes * E / (ms / 1e3) / 1e9
     h2d_rate = bin_ / (ms / E / 1e3) / 1e9
-    # host-side lower bound of one step on this GPU while every GPU copies, then the job's
+    # host-side lower bound of one step on this GPU while every GPU copies, then the
+    # job's: each direction at its own rate, both at the bidirectional rate, and the
+    # step's own mix of copies timed alone
     t_link = max(bin_ / (link["h2d_gbs"] * 1e9), bout / (link["d2h_gbs"] * 1e9),
-                 (bin_ + bout) / (link["bidirectional_gbs"] * 1e9))
+                 (bin_ + bout) / (link["bidirectional_gbs"] * 1e9), link["step_mix"]["s_per_step"])
     t_link = max_over_ranks([t_link])[0]
     roof = world * step_bytes / t_link / 1e9
     return {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": int(bin_), "d2h_bytes_per_step": int(bout),
@@ -1175,13 +1197,15 @@ def e2e(args, b, shape, dev, world, barrier, max_over_ranks):
             "host_gbs_achieved": round(world * (bin_ + bout) / (ms / E / 1e3) / 1e9, 1),
             "roofline": {"gbs": round(roof, 2), "ms_per_step": round(t_link * 1e3, 3),
                          "how": "max over GPUs of max(H2D bytes / H2D rate, D2H bytes / D2H rate, both / "
-                                "bidirectional rate), the rates measured with all GPUs copying at once"},
+                                "bidirectional rate, the time of the step's H2D and D2H bytes copied at once "
+                                "with nothing else running), all measured with every GPU copying at once"},
             "frac_of_link": round(gbs / roof, 3),
             "copies": "one H2D copy of the step's input arena and one D2H copy of its output arena" if arena else
                       f"one copy per tensor and chunk ({len(slices)} chunks over rows)",
             "how": "per step: pinned-host -> device copies of every input, the step's kernels, device -> pinned-host "
-                   "copies of every output, on three streams (chunks overlap copies and kernels); CUDA events, max "
-                   "over ranks; host buffers pinned after binding the rank to its GPU's NUMA-local CPUs"}
+                   "copies of every output, on three streams (chunks overlap copies and kernels, and a step's first "
+                   "chunks come in while the previous step's last chunks go out); CUDA events, max over ranks; "
+                   "host buffers pinned after binding the rank to its GPU's NUMA-local CPUs"}
 
 
 if __name__ == "__main__":
