@@ -7,7 +7,11 @@ One JSON line per shape on stdout. Inputs are seeded synthetic tensors of the
 Llama-3 8B / 70B decode and prefill shapes, resident on the GPU. The call is
 captured once in a CUDA graph (so the timed window holds GPU work only, not the
 host's launch path); each replay is preceded by a 256 MB write that evicts L2
-and timed alone with CUDA events on its stream (median of --reps). ``--once``
+and timed alone with CUDA events on its stream (median of --reps). That write
+leaves L2 full of dirty lines, which the timed call then writes back as it
+misses (up to 126 MB: ~19 us of DRAM time, a large share of a short call), so
+every shape is also timed after the write followed by a 256 MB read of another
+buffer, which leaves L2 holding clean lines only (``ms_clean_l2``). ``--once``
 makes two untimed calls per shape and nothing else (for profilers).
 
 attention: algorithmic bytes = the K and V rows every query reads plus q and the
@@ -64,10 +68,12 @@ def peaks():
         return (6650.0, "fallback"), (1590.0, "fallback")
 
 
-def time_call(fn, reps: int, dev) -> float:
+def time_call(fn, reps: int, dev, clean: bool = False) -> float:
     """Median milliseconds of one replay of fn() captured as a CUDA graph, over
-    reps replays, each after an L2-evicting write."""
+    reps replays, each after an L2-evicting write (clean: the write, then a read
+    of another buffer larger than L2, so no dirty line is left to write back)."""
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    reread = torch.ones(FLUSH_BYTES // 4, dtype=torch.float32, device=dev) if clean else None
     for _ in range(3):
         fn()
     torch.cuda.synchronize(dev)
@@ -79,6 +85,8 @@ def time_call(fn, reps: int, dev) -> float:
     times = []
     for _ in range(reps):
         flush.zero_()
+        if clean:
+            reread.sum()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         graph.replay()
@@ -122,6 +130,7 @@ def attention(names, reps: int, once: bool, dev) -> None:
             assert status.read() == 0
             continue
         ms = time_call(call, reps, dev)
+        ms_clean = time_call(call, reps, dev, clean=True)
         assert status.read() == 0, "device status set"
         es = q.element_size()
         nbytes = int(lens.sum().item()) * hkv * hd * es * 2 + 2 * q.numel() * es
@@ -132,7 +141,9 @@ def attention(names, reps: int, once: bool, dev) -> None:
             "kernel": "tcgen05" if es == 2 and hd == 128 else "cuda cores",
             "ms": round(ms, 4), "algorithmic_bytes": nbytes, "gbs": round(gbs, 1),
             "roofline": {"bound": "hbm", "peak": hbm, "peak_source": hbm_src, "frac": round(gbs / hbm, 4)},
-            "l2": "flushed before each call", "timing": "CUDA-graph replay"}), flush=True)
+            "ms_clean_l2": round(ms_clean, 4), "frac_clean_l2": round(nbytes / (ms_clean / 1e3) / 1e9 / hbm, 4),
+            "l2": "flushed before each call (a 256 MB write; ms_clean_l2: the write and a 256 MB read)",
+            "timing": "CUDA-graph replay"}), flush=True)
         del kc, vc
         torch.cuda.empty_cache()
 
@@ -159,8 +170,11 @@ def ffn(names, reps: int, once: bool, dev) -> None:
             assert status.read() == 0
             continue
         ms = time_call(call, reps, dev)
+        ms_clean = time_call(call, reps, dev, clean=True)
         assert status.read() == 0, "device status set"
-        cublas_ms = time_call(lambda: torch.nn.functional.silu(x @ wg) * (x @ wu), reps, dev)
+        cublas = lambda: torch.nn.functional.silu(x @ wg) * (x @ wu)  # noqa: E731
+        cublas_ms = time_call(cublas, reps, dev)
+        cublas_ms_clean = time_call(cublas, reps, dev, clean=True)
         flops = 2.0 * rows * dim * hidden * 2
         nbytes = (rows * dim + 2 * dim * hidden + rows * hidden) * 2
         tflops = flops / (ms / 1e3) / 1e12
@@ -172,7 +186,10 @@ def ffn(names, reps: int, once: bool, dev) -> None:
                          "frac": round(tflops / tf_peak, 4)},
             "cublas_matmul_plus_swiglu_ms": round(cublas_ms, 4),
             "cublas_tflops": round(flops / (cublas_ms / 1e3) / 1e12, 1),
-            "l2": "flushed before each call", "timing": "CUDA-graph replay"}), flush=True)
+            "ms_clean_l2": round(ms_clean, 4), "gbs_clean_l2": round(nbytes / (ms_clean / 1e3) / 1e9, 1),
+            "cublas_ms_clean_l2": round(cublas_ms_clean, 4),
+            "l2": "flushed before each call (a 256 MB write; *_clean_l2: the write and a 256 MB read)",
+            "timing": "CUDA-graph replay"}), flush=True)
         del x, wg, wu, out
         torch.cuda.empty_cache()
 
