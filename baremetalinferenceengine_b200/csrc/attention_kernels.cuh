@@ -318,11 +318,16 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(AttnArgs a) {
 }
 
 // One CTA of kCombineThreads per (query, q head): merges the splits' (max, sum,
-// output) partials. The splits' maxima and sums are read in parallel and turned
-// into per-split weights in shared memory (dynamic, one float per split), so each
-// output dimension is one pass of independent loads over the splits.
+// output) partials. Every load that needs no other result is issued at once:
+// thread s reads split s's maximum and sum, thread d the first kCombineChunk
+// splits' outputs of dimension d, so the partials cost one L2 round trip and two
+// barriers (the maximum, then the weights exp2(max_s - max) and the weighted sum).
+// The sums and products run in the same order as a split-by-split merge, so the
+// result does not depend on how the loads were grouped.
 constexpr int kCombineThreads = 128;
+constexpr int kCombineChunk = 16;  // output loads in flight per thread
 
+// Block-wide max or sum of v (NW warps); every thread gets the result.
 template <int NW>
 __device__ __forceinline__ float combine_block_reduce(float v, bool is_max, float* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -343,45 +348,64 @@ __device__ __forceinline__ float combine_block_reduce(float v, bool is_max, floa
 template <typename T>
 __global__ void __launch_bounds__(kCombineThreads) attention_combine_kernel(AttnArgs a) {
   grid_dependency_wait();
-  extern __shared__ float w_s[];  // [splits]
-  __shared__ float red[kCombineThreads / 32];
+  extern __shared__ float stats[];  // [splits] maxima, turned into weights; [splits] sums
+  __shared__ float red[2][kCombineThreads / 32];
   const int64_t b = blockIdx.y;
   const int h = blockIdx.x;
   int seq, len;
   if (check_query(a, b, &seq, &len)) return;  // reported by the split kernel
   const int kvh = h / a.group, g = h - kvh * a.group;
-  const int hd = a.hd, tid = threadIdx.x;
-  const float* base = a.ws + ((b * a.hkv + kvh) * a.splits * a.group + g) * static_cast<int64_t>(hd + 2);
+  const int hd = a.hd, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, S = a.splits;
+  const float* base = a.ws + ((b * a.hkv + kvh) * S * a.group + g) * static_cast<int64_t>(hd + 2);
   const int64_t split_stride = static_cast<int64_t>(a.group) * (hd + 2);
+  // An empty split writes only its maximum (-inf) and sum: its output slots hold
+  // whatever the workspace held before. They are loaded like the others (the
+  // addresses are inside the workspace) but never weighted, not even by 0.
+  float v[kCombineChunk];
+#pragma unroll
+  for (int j = 0; j < kCombineChunk; ++j) v[j] = (j < S && tid < hd) ? base[j * split_stride + tid] : 0.f;
   float m = -INFINITY;
-  for (int s = tid; s < a.splits; s += kCombineThreads) m = fmaxf(m, base[s * split_stride + hd]);
-  m = combine_block_reduce<kCombineThreads / 32>(m, true, red);  // finite: split 0 is never empty
-  float l = 0.f;
-  for (int s = tid; s < a.splits; s += kCombineThreads) {
-    const float ms = base[s * split_stride + hd];
-    const float w = ms == -INFINITY ? 0.f : exp2f(ms - m);
-    w_s[s] = w;
-    l += base[s * split_stride + hd + 1] * w;
+  for (int s = tid; s < S; s += kCombineThreads) {
+    const float ms = base[s * split_stride + hd], ls = base[s * split_stride + hd + 1];
+    stats[s] = ms;
+    stats[S + s] = ls;
+    m = fmaxf(m, ms);
   }
-  l = combine_block_reduce<kCombineThreads / 32>(l, false, red);  // its barriers also publish w_s
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if (lane == 0) red[0][warp] = m;
+  __syncthreads();
+  m = red[0][0];
+#pragma unroll
+  for (int w = 1; w < kCombineThreads / 32; ++w) m = fmaxf(m, red[0][w]);  // finite: split 0 is never empty
+  float l = 0.f;
+  for (int s = tid; s < S; s += kCombineThreads) {  // each thread its own splits: no barrier needed
+    const float ms = stats[s];
+    const float w = ms == -INFINITY ? 0.f : exp2f(ms - m);
+    stats[s] = w;
+    l += stats[S + s] * w;
+  }
+  l = warp_sum(l);
+  if (lane == 0) red[1][warp] = l;
+  __syncthreads();  // also publishes the weights
+  l = red[1][0];
+#pragma unroll
+  for (int w = 1; w < kCombineThreads / 32; ++w) l += red[1][w];
   T* out = static_cast<T*>(a.out) + (b * a.hq + h) * hd;
-  // an empty split writes only its maximum and sum: its output slots hold whatever
-  // the workspace held before, so they are never read, not weighted by 0
   for (int d = tid; d < hd; d += kCombineThreads) {
     float o = 0.f;
-    int s = 0;
-    for (; s + 8 <= a.splits; s += 8) {  // eight splits' loads in flight at once
-      float v[8];
+    for (int s0 = 0; s0 < S; s0 += kCombineChunk) {
+      if (s0 > 0 || d != tid) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = w_s[s + j] != 0.f ? base[(s + j) * split_stride + d] : 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (w_s[s + j] != 0.f) o = fmaf(v[j], w_s[s + j], o);
+        for (int j = 0; j < kCombineChunk; ++j) v[j] = s0 + j < S ? base[(s0 + j) * split_stride + d] : 0.f;
       }
-    }
-    for (; s < a.splits; ++s) {
-      const float w = w_s[s];
-      if (w != 0.f) o = fmaf(base[s * split_stride + d], w, o);
+#pragma unroll
+      for (int j = 0; j < kCombineChunk; ++j) {
+        if (s0 + j < S) {
+          const float w = stats[s0 + j];
+          if (w != 0.f) o = fmaf(v[j], w, o);
+        }
+      }
     }
     store1<T>(out + d, o / l);
   }
@@ -392,7 +416,7 @@ template <typename T>
 int launch_combine(const AttnArgs& a, cudaStream_t stream) {
   if (const int launch_status = launch_kernel("attention_combine_kernel", attention_combine_kernel<T>,
                                               dim3(dim3(a.hq, static_cast<unsigned>(a.batch))), dim3(kCombineThreads),
-                                              static_cast<size_t>(a.splits) * sizeof(float), stream, nullptr, a)) {
+                                              2 * static_cast<size_t>(a.splits) * sizeof(float), stream, nullptr, a)) {
     return launch_status;
   }
   return check_launch("bm_decode_attention (combine)");
