@@ -332,7 +332,9 @@ def config_dict(shape, n, scaling="weak", local=None):
             "kv_heads": shape.hkv, "head_dim": shape.hd, "ffn": shape.ffn, "vocab": shape.vocab,
             "rope_theta": shape.theta, "max_seq": shape.max_seq, "sequences": shape.num_seqs * (1 if strong else n),
             "sequences_per_gpu": local.num_seqs,
-            "l2": f"inputs larger than L2: {local.step_bytes() / 1e9:.2f} GB moved per step per GPU vs 126 MB L2"
+            "l2": f"inputs larger than L2: {local.step_bytes() / 1e9:.2f} GB moved per step per GPU vs 126 MB L2; "
+                  "the step is one CUDA graph replayed back to back; per-kernel times from steps launched one "
+                  "kernel at a time with events between launches"
                   if local.step_bytes() >= L2_RESIDENT_BYTES else
                   "L2-resident working set: the step is one CUDA graph replayed after a 256 MB write that "
                   "flushes L2; per-kernel times are per launch of a 16-launch graph (L2 warm)",
@@ -683,19 +685,34 @@ def main() -> int:
 
     launches = 0
     if not small:
-        # Inputs far larger than L2: K back-to-back steps, events between launches.
+        # Inputs far larger than L2: the step is one CUDA graph (its kernels chained
+        # by programmatic dependent launch, no host launch cost between them),
+        # replayed K times back to back; each kernel's own duration comes from K more
+        # steps launched one kernel at a time with events between the launches.
+        step_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(step_graph, stream=stream):
+            layer.run_step(b, stream)
+        with torch.cuda.stream(stream):
+            for _ in range(W):
+                step_graph.replay()
         events = [[torch.cuda.Event(enable_timing=True) for _ in range(nk + 1)] for _ in range(K)]
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
         torch.cuda.synchronize(dev)
         with ClockSampler(dev) as clocks:
-            start.record(stream)
-            for i in range(K):
-                launches += layer.run_step(b, stream, events[i])
-            end.record(stream)
+            with torch.cuda.stream(stream):
+                start.record(stream)
+                for i in range(K):
+                    step_graph.replay()
+                    launches += nk
+                end.record(stream)
             torch.cuda.synchronize(dev)
         barrier()
         elapsed_ms = start.elapsed_time(end)
+        for i in range(K):
+            layer.run_step(b, stream, events[i])
+        torch.cuda.synchronize(dev)
+        del step_graph
         per_kernel = [statistics.mean(events[i][j].elapsed_time(events[i][j + 1]) for i in range(K))
                       for j in range(nk)]
     else:
