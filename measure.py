@@ -1,13 +1,16 @@
 """Throughput of the tensor-core rows: decode attention and the fused FFN GEMM.
 
-    python measure.py attention [--shapes a,b] [--reps 20] [--once]
-    python measure.py ffn       [--shapes a,b] [--reps 10] [--once]
+    python measure.py attention [--shapes a,b] [--reps 50] [--once]
+    python measure.py ffn       [--shapes a,b] [--reps 20] [--once]
 
 One JSON line per shape on stdout. Inputs are seeded synthetic tensors of the
 Llama-3 8B / 70B decode and prefill shapes, resident on the GPU. The call is
 captured once in a CUDA graph (so the timed window holds GPU work only, not the
 host's launch path); each replay is preceded by a 256 MB write that evicts L2
-and timed alone with CUDA events on its stream (median of --reps). That write
+and timed alone with CUDA events on its stream (the mean of the middle 80 % of --reps:
+the B200's event timestamps advance in 2.05 µs steps, so a median of a ~20 µs call is
+one of a few values, while the mean of many replays, each starting at a different
+phase of the timer, resolves far below a step). That write
 leaves L2 full of dirty lines, which the timed call then writes back as it
 misses (up to 126 MB: ~19 us of DRAM time, a large share of a short call), so
 every shape is also timed after the write followed by a 256 MB read of another
@@ -26,7 +29,6 @@ import argparse
 import ctypes
 import json
 import os
-import statistics
 import sys
 
 REPO = os.path.dirname(os.path.abspath(__file__))
@@ -68,10 +70,18 @@ def peaks():
         return (6650.0, "fallback"), (1590.0, "fallback")
 
 
+def trimmed_mean(times, cut: float = 0.1) -> float:
+    """Mean of the values left after dropping the lowest and highest `cut` share."""
+    t = sorted(times)
+    k = int(len(t) * cut)
+    t = t[k:len(t) - k] or t
+    return sum(t) / len(t)
+
+
 def time_call(fn, reps: int, dev, clean: bool = False) -> float:
-    """Median milliseconds of one replay of fn() captured as a CUDA graph, over
-    reps replays, each after an L2-evicting write (clean: the write, then a read
-    of another buffer larger than L2, so no dirty line is left to write back)."""
+    """Milliseconds of one replay of fn() captured as a CUDA graph (trimmed mean
+    over reps replays), each after an L2-evicting write (clean: the write, then a
+    read of another buffer larger than L2, so no dirty line is left to write back)."""
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     reread = torch.ones(FLUSH_BYTES // 4, dtype=torch.float32, device=dev) if clean else None
     for _ in range(3):
@@ -93,7 +103,7 @@ def time_call(fn, reps: int, dev, clean: bool = False) -> float:
         e1.record()
         e1.synchronize()
         times.append(e0.elapsed_time(e1))
-    return statistics.median(times)
+    return trimmed_mean(times)
 
 
 def attention(names, reps: int, once: bool, dev) -> None:
@@ -209,9 +219,9 @@ def main(argv=None) -> int:
         if n not in table:
             raise SystemExit(f"unknown shape {n}; choose from {', '.join(table)}")
     if args.row == "attention":
-        attention(names, args.reps or 20, args.once, dev)
+        attention(names, args.reps or 50, args.once, dev)
     else:
-        ffn(names, args.reps or 10, args.once, dev)
+        ffn(names, args.reps or 20, args.once, dev)
     return 0
 
 
