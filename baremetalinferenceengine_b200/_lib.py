@@ -76,6 +76,8 @@ SIGNATURES = {
     "bm_gemm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_int, c_void_p, c_void_p]),
     "bm_gemm_shared_a": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int64, c_int32, c_int, c_void_p,
                                  c_void_p]),
+    "bm_rmsnorm_gemm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_void_p,
+                                c_void_p, c_int32, c_int32, c_int64, c_int32, c_int, c_void_p, c_void_p]),
     "bm_softmax": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p]),
     "bm_decode_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int64,
                                     c_int32, c_int32, c_int32, c_int32, c_int32, c_float, c_void_p, ctypes.c_size_t,

@@ -63,6 +63,13 @@ int gemm_f32_shared_a(float* const* c, const float* a, const float* const* b, co
 // out[rows][hidden] = silu(x w_gate) * (x w_up), x [rows][dim], w_* [dim][hidden].
 int gemm_f32_swiglu(float* out, const float* x, const float* w_gate, const float* w_up, int64_t rows, int hidden,
                     int dim, cudaStream_t stream);
+// The same products of y = rmsnorm(h + d) * norm_w (d may be null), y made in the
+// kernel's prologue; residual_out (may be null) receives h + d. swiglu: b[0], b[1]
+// are the gate and up weights (n[0] == n[1]) and c[0] the one output. Rows too long
+// for shared memory run the norm into `normed` first (two or three launches).
+int gemm_f32_norm(float* const* c, const float* h, const float* d, const float* norm_w, float eps,
+                  float* residual_out, float* normed, const float* const* b, const int32_t* n, int count,
+                  bool swiglu, int64_t m, int k, cudaStream_t stream);
 
 // cudaFuncSetAttribute(kernel, MaxDynamicSharedMemorySize, bytes) on the current
 // device, once per (device, kernel): later calls cost a lookup, not a driver call.

@@ -834,3 +834,55 @@ extern "C" int bm_gemm_shared_a(void* const* c, const void* a, const void* const
   }
   return BM_OK;
 }
+
+extern "C" int bm_rmsnorm_gemm(void* const* c, const void* h, const void* d, const void* norm_weight, float eps,
+                               void* residual_out, void* normed, const void* const* b, const int32_t* n,
+                               int32_t count, int32_t swiglu, int64_t m, int32_t k, bm_dtype_t dtype,
+                               int32_t* d_status, void* stream) {
+  using namespace bm;
+  const char* what = "bm_rmsnorm_gemm";
+  if (!valid_dtype(dtype)) return fail(BM_ERR_INVALID_ARGUMENT, "%s: bad dtype", what);
+  if (!c || !b || !n) return fail(BM_ERR_INVALID_ARGUMENT, "%s: NULL array", what);
+  if (swiglu ? count != 2 : (count < 1 || count > kMaxSharedA)) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: count must be 2 with swiglu, else 1 to 3", what);
+  }
+  if (m < 0 || m > (int64_t{1} << 31) || k <= 0) return fail(BM_ERR_INVALID_ARGUMENT, "%s: bad size", what);
+  if (swiglu && n[0] != n[1]) return fail(BM_ERR_INVALID_ARGUMENT, "%s: gate and up widths differ", what);
+  for (int o = 0; o < count; ++o) {
+    if (n[o] < 0) return fail(BM_ERR_INVALID_ARGUMENT, "%s: negative width", what);
+    if (m > 0 && n[o] > 0 && (!b[o] || ((o == 0 || !swiglu) && !c[o]))) {
+      return fail(BM_ERR_INVALID_ARGUMENT, "%s: NULL pointer", what);
+    }
+  }
+  if (m == 0) return BM_OK;
+  if (!h || !norm_weight || !normed) return fail(BM_ERR_INVALID_ARGUMENT, "%s: NULL pointer", what);
+  const size_t row_bytes = static_cast<size_t>(k) * dtype_size(dtype), bytes = row_bytes * static_cast<size_t>(m);
+  auto overlaps = [bytes](const void* x, const void* y) {
+    const char *p = static_cast<const char*>(x), *q = static_cast<const char*>(y);
+    return x != nullptr && y != nullptr && p < q + bytes && q < p + bytes;
+  };
+  if (overlaps(residual_out, h) || overlaps(residual_out, d)) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: residual_out overlaps h or d", what);
+  }
+  if (dtype == BM_F32) {
+    return gemm_f32_norm(reinterpret_cast<float* const*>(c), static_cast<const float*>(h),
+                         static_cast<const float*>(d), static_cast<const float*>(norm_weight), eps,
+                         static_cast<float*>(residual_out), static_cast<float*>(normed),
+                         reinterpret_cast<const float* const*>(b), n, count, swiglu != 0, m, k, as_stream(stream));
+  }
+  // bf16: the norm (with the add) into `normed`, then the tensor-core products
+  int st;
+  if (d != nullptr && residual_out != nullptr) {
+    const cudaError_t err = cudaMemcpyAsync(residual_out, h, bytes, cudaMemcpyDeviceToDevice, as_stream(stream));
+    if (err != cudaSuccess) return fail(BM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+    st = bm_add_rmsnorm(residual_out, d, norm_weight, normed, m, k, eps, dtype, stream);
+  } else if (d != nullptr) {
+    st = bm_add(normed, h, d, m * static_cast<int64_t>(k), dtype, stream);
+    if (st == BM_OK) st = bm_rmsnorm(normed, normed, norm_weight, m, k, eps, k, k, dtype, stream);
+  } else {
+    st = bm_rmsnorm(normed, h, norm_weight, m, k, eps, k, k, dtype, stream);
+  }
+  if (st != BM_OK) return st;
+  if (swiglu) return bm_gemm_swiglu(c[0], normed, b[0], b[1], m, k, n[0], dtype, d_status, stream);
+  return bm_gemm_shared_a(c, normed, b, n, count, m, k, dtype, d_status, stream);
+}

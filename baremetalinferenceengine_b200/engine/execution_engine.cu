@@ -3,6 +3,7 @@
 
 #include <iostream>
 #include <stdexcept>
+#include <utility>
 
 #include "bm_layer_ops.h"
 #include "kernels.cuh"
@@ -66,6 +67,7 @@ void ExecutionEngine::reserve(int tokens) {
     return activations_.back()->get();
   };
   hidden_ = buffer(n * dim);
+  hidden_alt_ = buffer(n * dim);
   normed_ = buffer(n * dim);
   q_ = buffer(n * dim);
   k_ = buffer(n * dim);
@@ -168,25 +170,27 @@ void ExecutionEngine::run(int T, int max_len) {
                         stream_),
         "bm_embed_gather");
 
+  // The residual stream alternates between hidden_ and hidden_alt_: every residual
+  // add is fused into the norm of the product that follows it (bm_rmsnorm_gemm), whose
+  // kernel still reads the old rows while it writes the new ones.
+  float* h = hidden_;
+  float* h_next = hidden_alt_;
   for (int l = 0; l < config_.num_layers; ++l) {
     const LayerWeights& w = layers_[l];
     float* k_cache = kv_cache_->get_key_cache(l);
     float* v_cache = kv_cache_->get_value_cache(l);
 
-    // The previous layer's residual add (its down projection) is fused into this norm.
-    if (l == 0) {
-      check(bm_rmsnorm(normed_, hidden_, w.attention_norm, T, dim, eps, dim, dim, BM_F32, stream_), "bm_rmsnorm");
-    } else {
-      check(bm_add_rmsnorm(hidden_, projected_, w.attention_norm, normed_, T, dim, eps, BM_F32, stream_),
-            "bm_add_rmsnorm");
-    }
-    // Q, K and V projections of the same normed rows: one launch
+    // The previous layer's residual add (its down projection), this layer's attention
+    // norm (:109, :80 for layer 0) and the Q, K and V projections (:110-112): one launch.
     {
       void* outs[3] = {q_, k_, v_};
       const void* weights[3] = {w.q_proj, w.k_proj, w.v_proj};
       const int32_t widths[3] = {dim, dim, dim};
-      check(bm_gemm_shared_a(outs, normed_, weights, widths, 3, T, dim, BM_F32, nullptr, stream_),
-            "bm_gemm_shared_a");
+      const float* delta = l == 0 ? nullptr : projected_;
+      check(bm_rmsnorm_gemm(outs, h, delta, w.attention_norm, eps, delta ? h_next : nullptr, normed_, weights,
+                            widths, 3, 0, T, dim, BM_F32, nullptr, stream_),
+            "bm_rmsnorm_gemm");
+      if (delta) std::swap(h, h_next);
     }
     // Token t at cache position positions_[t] of the one sequence the reference's cache holds.
     check(bm_rope_kv_store(q_, k_, v_, positions_, 0, nullptr, k_cache, v_cache, rope_table_->get(),
@@ -199,18 +203,30 @@ void ExecutionEngine::run(int T, int max_len) {
                               attention_workspace_->size(), BM_F32, nullptr, stream_),
           "bm_decode_attention");
     launch_gemm(projected_, attention_out_, w.o_proj, T, dim, dim, stream_);
-    check(bm_add_rmsnorm(hidden_, projected_, w.ffn_norm, normed_, T, dim, eps, BM_F32, stream_), "bm_add_rmsnorm");
-    // gate and up projections with the SwiGLU in the epilogue (:122-124): one launch
-    check(bm_gemm_swiglu(activated_, normed_, w.gate_proj, w.up_proj, T, dim, hidden_dim, BM_F32, nullptr, stream_),
-          "bm_gemm_swiglu");
+    // The attention residual add (:118), the FFN norm (:121) and the gate and up
+    // projections with the SwiGLU in the epilogue (:122-124): one launch.
+    {
+      void* outs[2] = {activated_, nullptr};
+      const void* weights[2] = {w.gate_proj, w.up_proj};
+      const int32_t widths[2] = {hidden_dim, hidden_dim};
+      check(bm_rmsnorm_gemm(outs, h, projected_, w.ffn_norm, eps, h_next, normed_, weights, widths, 2, 1, T, dim,
+                            BM_F32, nullptr, stream_),
+            "bm_rmsnorm_gemm");
+      std::swap(h, h_next);
+    }
     launch_gemm(projected_, activated_, w.down_proj, T, dim, hidden_dim, stream_);
   }
 
-  // Only the last token's logits are returned: its final residual add and norm.
+  // Only the last token's logits are returned: its final residual add and norm with
+  // the vocabulary product, one launch.
   const size_t last = static_cast<size_t>(T - 1) * dim;
-  check(bm_add_rmsnorm(hidden_ + last, projected_ + last, final_norm_, normed_ + last, 1, dim, eps, BM_F32,
-                       stream_),
-        "bm_add_rmsnorm");
-  launch_gemm(logits_->get(), normed_ + last, lm_head_, 1, config_.vocab_size, dim, stream_);
+  {
+    void* outs[1] = {logits_->get()};
+    const void* weights[1] = {lm_head_};
+    const int32_t widths[1] = {config_.vocab_size};
+    check(bm_rmsnorm_gemm(outs, h + last, projected_ + last, final_norm_, eps, nullptr, normed_ + last, weights,
+                          widths, 1, 0, 1, dim, BM_F32, nullptr, stream_),
+          "bm_rmsnorm_gemm");
+  }
 }
 

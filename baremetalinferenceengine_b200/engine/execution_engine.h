@@ -80,8 +80,9 @@ class ExecutionEngine {
   // [capacity][dim] / [capacity][hidden_dim] activations, fp32
   int capacity_ = 0;
   std::vector<std::shared_ptr<DeviceBuffer<float>>> activations_;
-  float* hidden_ = nullptr;
-  float* normed_ = nullptr;
+  float* hidden_ = nullptr;    // the residual stream; each add writes the other buffer of the pair
+  float* hidden_alt_ = nullptr;
+  float* normed_ = nullptr;    // norm output, for rows too long to normalise inside a product
   float* q_ = nullptr;
   float* k_ = nullptr;
   float* v_ = nullptr;

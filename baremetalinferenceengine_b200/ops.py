@@ -270,6 +270,56 @@ def gemm_shared_a(a: torch.Tensor, bs, outs=None, status: Optional[DeviceStatus]
     return outs
 
 
+def rmsnorm_gemm(h: torch.Tensor, norm_weight: torch.Tensor, bs, d: Optional[torch.Tensor] = None, eps: float = 1e-5,
+                 swiglu: bool = False, outs=None, residual_out: Optional[torch.Tensor] = None,
+                 normed: Optional[torch.Tensor] = None, status: Optional[DeviceStatus] = None, stream=None):
+    """The norm before a projection and the projection: y = rmsnorm(h + d) * norm_weight
+    (d optional), then [y @ b for b in bs] (one to three weights), or with swiglu
+    (bs = [w_gate, w_up]) the one output silu(y @ w_gate) * (y @ w_up). residual_out,
+    when given with d, receives h + d. fp32 rows that fit run as one launch."""
+    _dense(h, "h")
+    bs = list(bs)
+    if h.dim() != 2:
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "need h [m, k]")
+    m, k = h.shape
+    if (len(bs) != 2) if swiglu else not 1 <= len(bs) <= 3:
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "two weights with swiglu, else one to three")
+    for b in bs:
+        _dense(b, "b")
+        if b.dim() != 2 or b.shape[0] != k:
+            raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "need every b [k, n]")
+    widths = [b.shape[1] for b in bs]
+    n_out = 1 if swiglu else len(bs)
+    if outs is None:
+        outs = [torch.empty((m, widths[o]), dtype=h.dtype, device=h.device) for o in range(n_out)]
+    outs = list(outs)
+    if len(outs) != n_out:
+        raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "one output per product (one with swiglu)")
+    for o, out in enumerate(outs):
+        _dense(out, "out")
+        if tuple(out.shape) != (m, widths[o]):
+            raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "every out must be [m, n]")
+    if normed is None:
+        normed = torch.empty_like(h)
+    extra = [t for t in (d, residual_out) if t is not None]
+    for t in extra + [normed]:
+        _dense(t, "h-shaped tensor")
+        if tuple(t.shape) != (m, k):
+            raise BMError(_lib.BM_ERR_INVALID_ARGUMENT, "d, residual_out and normed must be [m, k]")
+    _dense(norm_weight, "norm_weight")
+    _same(h, norm_weight, *bs, *outs, normed, *extra)
+    count = len(bs)
+    c_arr = (ctypes.c_void_p * count)(*([_ptr(o) for o in outs] + [None] * (count - len(outs))))
+    b_arr = (ctypes.c_void_p * count)(*[_ptr(b) for b in bs])
+    n_arr = (ctypes.c_int32 * count)(*widths)
+    with torch.cuda.device(_dev(h)):
+        check(load().bm_rmsnorm_gemm(c_arr, _ptr(h), _ptr(d), _ptr(norm_weight), eps,
+                                     _ptr(residual_out), _ptr(normed), b_arr,
+                                     n_arr, count, int(swiglu), m, k, bm_dtype(h), status.ptr if status else None,
+                                     _stream(h.device, stream)))
+    return outs
+
+
 def softmax(x: torch.Tensor, size: Optional[int] = None, num_vectors: int = 1, stride: Optional[int] = None,
             stream=None) -> torch.Tensor:
     """In place: num_vectors vectors of `size` elements, `stride` apart, each

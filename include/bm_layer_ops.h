@@ -321,6 +321,25 @@ int bm_gemm(void* c, const void* a, const void* b, int64_t m, int32_t n, int32_t
 int bm_gemm_shared_a(void* const* c, const void* a, const void* const* b, const int32_t* n, int32_t count,
                      int64_t m, int32_t k, bm_dtype_t dtype, int32_t* d_status, void* stream);
 
+/* The RMSNorm before a projection and the projection together (the norms of
+ * src/execution_engine.cu:80,109,121, after the residual adds of :118,126, each
+ * followed by its products :81,110-112,122-123):
+ *   x = h + d                      (d may be NULL: x = h)
+ *   y = x * rsqrt(mean(x^2) + eps) * norm_weight       (as bm_rmsnorm computes it)
+ *   swiglu == 0: c[o] = y . b[o] for o < count (1 to 3)   (as bm_gemm_shared_a)
+ *   swiglu != 0: count 2, c[0] = silu(y . b[0]) * (y . b[1])   (as bm_gemm_swiglu)
+ * h, d, residual_out and normed are [m][k]; b[o] is [k][n[o]]. residual_out
+ * (may be NULL) receives x, the updated residual stream, when d is given; it must
+ * not overlap h or d, which the kernel still reads while it is written.
+ * BM_F32 with the normalised rows of a CTA's share of K fitting its shared memory
+ * (one-token and few-token products): ONE launch, y never written to memory (its
+ * sum of squares is ordered as the product kernel's threads hold the row, so y can
+ * differ from bm_rmsnorm's in the last bit). Otherwise, and for BM_BF16, the norm
+ * runs first into `normed` (scratch, always required), then the products. k > 0. */
+int bm_rmsnorm_gemm(void* const* c, const void* h, const void* d, const void* norm_weight, float eps,
+                    void* residual_out, void* normed, const void* const* b, const int32_t* n, int32_t count,
+                    int32_t swiglu, int64_t m, int32_t k, bm_dtype_t dtype, int32_t* d_status, void* stream);
+
 /* Softmax in place over num_vectors vectors of `size` elements, `stride`
  * elements apart (the gaps untouched): x = exp(x - max) / sum exp(x - max), fp32
  * arithmetic. Replaces launch_softmax(_batch) (include/kernels.cuh:23-26,
