@@ -78,6 +78,10 @@ SIGNATURES = {
                                  c_void_p]),
     "bm_rmsnorm_gemm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_void_p,
                                 c_void_p, c_int32, c_int32, c_int64, c_int32, c_int, c_void_p, c_void_p]),
+    "bm_rope_kv_decode_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32,
+                                            c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int64, c_int32, c_int32,
+                                            c_int32, c_int32, c_int32, c_float, c_void_p, ctypes.c_size_t, c_int,
+                                            c_void_p, c_void_p]),
     "bm_softmax": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p]),
     "bm_decode_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int64,
                                     c_int32, c_int32, c_int32, c_int32, c_int32, c_float, c_void_p, ctypes.c_size_t,

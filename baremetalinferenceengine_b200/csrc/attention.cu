@@ -129,6 +129,25 @@ int grid_min_tiles(const AttnArgs& a, bm_dtype_t dtype) {
   return tc_eligible(a, dtype) || f32_tma_eligible(a, dtype) ? kStagedMinTiles : kCudaCoreMinTiles;
 }
 
+// The per-(query, kv head, split) grid's plan: splits sized for the GPU, cut back
+// to what the caller's workspace holds (maybe one split per pair).
+void plan_grid(AttnArgs& a, void* workspace, size_t workspace_size, bm_dtype_t dtype) {
+  const int64_t batch = a.batch;
+  const int hkv = a.hkv, hd = a.hd, max_len = a.max_len;
+  plan_splits(batch * hkv, max_len, sm_count(), &a.splits, &a.split_len, grid_min_tiles(a, dtype));
+  const size_t need = workspace_bytes(batch, hkv, a.group, hd, a.splits);
+  if (need > 0 && (workspace == nullptr || workspace_size < need)) {
+    // Less scratch than the plan wants: as many splits as it holds (maybe one).
+    const size_t per_split = workspace_bytes(batch, hkv, a.group, hd, 2) / 2;
+    const int fit = workspace == nullptr ? 1 : static_cast<int>(std::min<size_t>(workspace_size / per_split, a.splits));
+    const int tiles = (max_len + kThreads - 1) / kThreads;
+    const int tiles_per_split = (tiles + std::max(fit, 1) - 1) / std::max(fit, 1);
+    a.split_len = tiles_per_split * kThreads;
+    a.splits = (tiles + tiles_per_split - 1) / tiles_per_split;
+  }
+  a.ws = a.splits > 1 ? static_cast<float*>(workspace) : nullptr;
+}
+
 }  // namespace
 
 int decode_attention(void* out, const void* q, const void* k_cache, const void* v_cache, const int32_t* seq_ids,
@@ -152,21 +171,45 @@ int decode_attention(void* out, const void* q, const void* k_cache, const void* 
       return launch_tc_balanced(a, ctas, s);
     }
   }
-  plan_splits(batch * hkv, max_len, sm_count(), &a.splits, &a.split_len, grid_min_tiles(a, dtype));
-  const size_t need = workspace_bytes(batch, hkv, a.group, hd, a.splits);
-  if (need > 0 && (workspace == nullptr || workspace_size < need)) {
-    // Less scratch than the plan wants: as many splits as it holds (maybe one).
-    const size_t per_split = workspace_bytes(batch, hkv, a.group, hd, 2) / 2;
-    const int fit = workspace == nullptr ? 1 : static_cast<int>(std::min<size_t>(workspace_size / per_split, a.splits));
-    const int tiles = (max_len + kThreads - 1) / kThreads;
-    const int tiles_per_split = (tiles + std::max(fit, 1) - 1) / std::max(fit, 1);
-    a.split_len = tiles_per_split * kThreads;
-    a.splits = (tiles + tiles_per_split - 1) / tiles_per_split;
-  }
-  a.ws = a.splits > 1 ? static_cast<float*>(workspace) : nullptr;
+  plan_grid(a, workspace, workspace_size, dtype);
   if (tc) return launch_tc(a, s);
   if (f32_tma_eligible(a, dtype)) return launch_f32_tma(a, s);
   return dtype == BM_F32 ? launch_f32(a, s) : launch_bf16(a, s);
+}
+
+int rope_kv_decode_attention(void* out, void* q, const void* k, const void* v, const int32_t* positions,
+                             const void* rope_table, int32_t table_len, const int32_t* seq_ids, void* k_cache,
+                             void* v_cache, const int32_t* lens, int32_t max_len, int64_t batch, int32_t hq,
+                             int32_t hkv, int32_t hd, int32_t max_seq, int32_t num_seqs, float scale, void* workspace,
+                             size_t workspace_size, bm_dtype_t dtype, int32_t* d_status, void* stream) {
+  const char* what = "bm_rope_kv_decode_attention";
+  if (int st = check_call(what, out, q, k_cache, v_cache, batch, hq, hkv, hd, max_seq, num_seqs, max_len, dtype)) {
+    return st;
+  }
+  if (batch == 0) return BM_OK;
+  if (!k || !v || !positions || !lens || !rope_table) return fail(BM_ERR_INVALID_ARGUMENT, "%s: NULL pointer", what);
+  if (hd % 2 != 0 || table_len <= 0 || reinterpret_cast<uintptr_t>(rope_table) % 8 != 0) {
+    return fail(BM_ERR_INVALID_ARGUMENT, "%s: need an even head_dim and an 8-byte aligned table", what);
+  }
+  AttnArgs a = fill_args(out, q, k_cache, v_cache, seq_ids, lens, 0, max_len, batch, hq, hkv, hd, max_seq, num_seqs,
+                         scale, d_status);
+  if (tc_eligible(a, dtype) || f32_tma_eligible(a, dtype)) {
+    // the staged kernels (head_dim 128) read the caches by TMA: the new rows go in first
+    if (int st = bm_rope_kv_store(q, k, v, positions, 0, seq_ids, k_cache, v_cache, rope_table, table_len, 0.0,
+                                  batch, hq, hkv, hd, max_seq, num_seqs, dtype, d_status, stream)) {
+      return st;
+    }
+    return decode_attention(out, q, k_cache, v_cache, seq_ids, lens, 0, max_len, batch, hq, hkv, hd, max_seq,
+                            num_seqs, scale, workspace, workspace_size, dtype, d_status, stream);
+  }
+  a.k_new = k;
+  a.v_new = v;
+  a.positions = positions;
+  a.rope_table = static_cast<const float2*>(rope_table);
+  a.rope_len = table_len;
+  plan_grid(a, workspace, workspace_size, dtype);
+  cudaStream_t s = as_stream(stream);
+  return dtype == BM_F32 ? launch_f32_rope(a, s) : launch_bf16_rope(a, s);
 }
 
 int decode_attention_scratch_need(const void* q, const void* k_cache, const void* v_cache, int32_t max_len,
@@ -222,4 +265,16 @@ extern "C" int bm_decode_attention(void* out, const void* q, const void* k_cache
   if (!lens) return bm::fail(BM_ERR_INVALID_ARGUMENT, "bm_decode_attention: NULL lens");
   return bm::decode_attention(out, q, k_cache, v_cache, seq_ids, lens, 0, max_len, batch, num_q_heads, num_kv_heads,
                               head_dim, max_seq, num_seqs, scale, workspace, workspace_bytes, dtype, d_status, stream);
+}
+
+extern "C" int bm_rope_kv_decode_attention(void* out, void* q, const void* k, const void* v,
+                                           const int32_t* positions, const void* rope_table, int32_t rope_table_len,
+                                           const int32_t* seq_ids, void* k_cache, void* v_cache, const int32_t* lens,
+                                           int32_t max_len, int64_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                           int32_t head_dim, int32_t max_seq, int32_t num_seqs, float scale,
+                                           void* workspace, size_t workspace_bytes, bm_dtype_t dtype,
+                                           int32_t* d_status, void* stream) {
+  return bm::rope_kv_decode_attention(out, q, k, v, positions, rope_table, rope_table_len, seq_ids, k_cache, v_cache,
+                                      lens, max_len, batch, num_q_heads, num_kv_heads, head_dim, max_seq, num_seqs,
+                                      scale, workspace, workspace_bytes, dtype, d_status, stream);
 }

@@ -5,6 +5,7 @@ namespace bm {
 namespace attn {
 
 int launch_f32(const AttnArgs& a, cudaStream_t stream) { return launch<float>(a, stream); }
+int launch_f32_rope(const AttnArgs& a, cudaStream_t stream) { return launch<float, true>(a, stream); }
 
 }  // namespace attn
 }  // namespace bm

@@ -33,6 +33,13 @@ struct AttnArgs {
   float qscale;           // log2(e) * softmax scale
   float* ws;              // [batch][hkv][splits][group][hd + 2]: o..., m, l
   int32_t* status;
+  // ROPE form (bm_rope_kv_decode_attention): each query's new token is rotated and
+  // stored in the cache by the CTA that attends to its position, before it attends
+  const void* k_new;          // [batch][hkv][hd], not yet rotated
+  const void* v_new;          // [batch][hkv][hd]
+  const int32_t* positions;   // [batch]: the new token's cache position
+  const float2* rope_table;   // [rope_len][hd / 2] (cos, sin)
+  int rope_len;
 };
 
 __device__ __forceinline__ int query_len(const AttnArgs& a, int64_t b) { return a.lens ? a.lens[b] : a.len0; }
@@ -79,20 +86,31 @@ __device__ __forceinline__ void block_reduce(float (&vals)[GM], int G, float (*s
   __syncthreads();
 }
 
+// A cache load: the read-only path, or (COHERENT) one served by L2, for a cache
+// that the same kernel writes (the ROPE form stores the new token's rows first).
+template <bool COHERENT, typename V>
+__device__ __forceinline__ V ld_cache(const V* p) {
+  if constexpr (COHERENT) {
+    return __ldcg(p);
+  } else {
+    return __ldg(p);
+  }
+}
+
 // Loads N consecutive elements of T (N * sizeof(T) a power of two from 2 to 32
 // bytes, aligned to the smaller of that size and 16) as floats.
-template <typename T, int N>
+template <typename T, int N, bool COHERENT = false>
 __device__ __forceinline__ void load_n(const T* p, float* f) {
   constexpr int kBytes = N * static_cast<int>(sizeof(T));
   static_assert(kBytes == 2 || kBytes == 4 || kBytes == 8 || kBytes == 16 || kBytes == 32, "unsupported width");
   if constexpr (kBytes == 32) {
     constexpr int kHalf = 16 / static_cast<int>(sizeof(T));
-    unpack16<T>(__ldg(reinterpret_cast<const uint4*>(p)), f);
-    unpack16<T>(__ldg(reinterpret_cast<const uint4*>(p + kHalf)), f + kHalf);
+    unpack16<T>(ld_cache<COHERENT>(reinterpret_cast<const uint4*>(p)), f);
+    unpack16<T>(ld_cache<COHERENT>(reinterpret_cast<const uint4*>(p + kHalf)), f + kHalf);
   } else if constexpr (kBytes == 16) {
-    unpack16<T>(__ldg(reinterpret_cast<const uint4*>(p)), f);
+    unpack16<T>(ld_cache<COHERENT>(reinterpret_cast<const uint4*>(p)), f);
   } else if constexpr (kBytes == 8) {
-    const uint2 r = __ldg(reinterpret_cast<const uint2*>(p));
+    const uint2 r = ld_cache<COHERENT>(reinterpret_cast<const uint2*>(p));
     if constexpr (sizeof(T) == 4) {
       f[0] = __uint_as_float(r.x);
       f[1] = __uint_as_float(r.y);
@@ -103,7 +121,7 @@ __device__ __forceinline__ void load_n(const T* p, float* f) {
       f[3] = bf16_hi(r.y);
     }
   } else if constexpr (kBytes == 4) {
-    const uint32_t r = __ldg(reinterpret_cast<const unsigned int*>(p));
+    const uint32_t r = ld_cache<COHERENT>(reinterpret_cast<const unsigned int*>(p));
     if constexpr (sizeof(T) == 4) {
       f[0] = __uint_as_float(r);
     } else {
@@ -119,7 +137,14 @@ __device__ __forceinline__ void load_n(const T* p, float* f) {
 // it); DPL = ceil(head_dim / 32) dimensions per lane in the mix. CONTIG (head_dim
 // = 32 * DPL, DPL a power of two): lane l owns dimensions [l*DPL, l*DPL + DPL)
 // and reads them with one vector load; otherwise it owns l, l + 32, ...
-template <typename T, int GM, int DPL, bool CONTIG>
+//
+// ROPE: the query's new token comes unrotated (q, k_new, v_new at positions[b]).
+// Every CTA rotates the group's queries as it stages them; the CTA whose split
+// holds the position also rotates k_new into the K cache and copies v_new into the
+// V cache there, then reads the caches through L2 (its own stores included). The
+// rotation and the stored values are those of bm_rope_kv_store (rope_rotate, the
+// rotated q rounded to T as it would be stored), so the output is the two calls'.
+template <typename T, int GM, int DPL, bool CONTIG, bool ROPE = false>
 __global__ void __launch_bounds__(kThreads) attention_split_kernel(AttnArgs a) {
   grid_dependency_wait();
   constexpr int VEC = VecWidth<T>::value;
@@ -155,14 +180,51 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(AttnArgs a) {
     return;
   }
 
+  const int64_t head_base = (static_cast<int64_t>(seq) * a.hkv + kvh) * a.max_seq * hd;
   // queries of the group, pre-scaled, in shared memory
   const T* qb = static_cast<const T*>(a.q) + (b * a.hq + static_cast<int64_t>(kvh) * G) * hd;
-  for (int i = tid; i < G * hd; i += kThreads) q_s[i] = load1<T>(qb + i) * a.qscale;
+  if constexpr (ROPE) {
+    const int half = hd / 2;
+    int pos = a.positions[b];
+    if (pos < 0 || pos >= len || pos >= a.rope_len) {  // nothing rotated or stored, as bm_rope_kv_store skips it
+      if (tid == 0 && kvh == 0 && split == 0) raise_status(a.status, BM_DEVERR_BAD_POSITION);
+      pos = -1;
+    }
+    float2* cs = reinterpret_cast<float2*>(red);  // (cos, sin) of pos: red is free until the end
+    if (pos >= 0) {
+      for (int i = tid; i < half; i += kThreads) cs[i] = __ldg(a.rope_table + static_cast<int64_t>(pos) * half + i);
+    }
+    __syncthreads();
+    for (int i = tid; i < G * hd; i += kThreads) {
+      float x = load1<T>(qb + i);
+      if (pos >= 0) {
+        const int g = i / hd, d = i - g * hd, pr = d < half ? d : d - half;
+        float o1, o2;
+        rope_rotate(load1<T>(qb + g * hd + pr), load1<T>(qb + g * hd + pr + half), cs[pr], &o1, &o2);
+        x = round_to<T>(d < half ? o1 : o2);
+      }
+      q_s[i] = x * a.qscale;
+    }
+    if (pos >= start && pos < end) {  // this split attends to the new position: its K and V rows go in first
+      const T* kn = static_cast<const T*>(a.k_new) + (b * a.hkv + kvh) * static_cast<int64_t>(hd);
+      const T* vn = static_cast<const T*>(a.v_new) + (b * a.hkv + kvh) * static_cast<int64_t>(hd);
+      T* kc = const_cast<T*>(static_cast<const T*>(a.k_cache)) + head_base + static_cast<int64_t>(pos) * hd;
+      T* vc = const_cast<T*>(static_cast<const T*>(a.v_cache)) + head_base + static_cast<int64_t>(pos) * hd;
+      for (int d = tid; d < hd; d += kThreads) {
+        const int pr = d < half ? d : d - half;
+        float o1, o2;
+        rope_rotate(load1<T>(kn + pr), load1<T>(kn + pr + half), cs[pr], &o1, &o2);
+        store1<T>(kc + d, d < half ? o1 : o2);
+        vc[d] = vn[d];
+      }
+    }
+  } else {
+    for (int i = tid; i < G * hd; i += kThreads) q_s[i] = load1<T>(qb + i) * a.qscale;
+  }
   if (tid < G) {
     m_s[tid] = -INFINITY;
     l_s[tid] = 0.f;
   }
-  const int64_t head_base = (static_cast<int64_t>(seq) * a.hkv + kvh) * a.max_seq * hd;
   const T* kbase = static_cast<const T*>(a.k_cache) + head_base;
   const T* vbase = static_cast<const T*>(a.v_cache) + head_base;
   auto dim_of = [&](int i) { return CONTIG ? lane * DPL + i : lane + 32 * i; };
@@ -188,7 +250,7 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(AttnArgs a) {
         uint4 kr[KB];
 #pragma unroll
         for (int c = 0; c < KB; ++c) {
-          if ((cb + c) * VEC < hd) kr[c] = __ldg(reinterpret_cast<const uint4*>(krow + (cb + c) * VEC));
+          if ((cb + c) * VEC < hd) kr[c] = ld_cache<ROPE>(reinterpret_cast<const uint4*>(krow + (cb + c) * VEC));
         }
 #pragma unroll
         for (int c = 0; c < KB; ++c) {
@@ -260,7 +322,7 @@ __global__ void __launch_bounds__(kThreads) attention_split_kernel(AttnArgs a) {
         const int j = j0 + u * kWarps;
         const T* vrow = vbase + static_cast<int64_t>(tile + min(j, tile_end - 1)) * hd;
         if constexpr (CONTIG) {
-          load_n<T, DPL>(vrow + lane * DPL, v[u]);
+          load_n<T, DPL, ROPE>(vrow + lane * DPL, v[u]);
         } else {
 #pragma unroll
           for (int i = 0; i < DPL; ++i) {
@@ -425,7 +487,7 @@ int launch_combine(const AttnArgs& a, cudaStream_t stream) {
 // Splits for `pairs` (query, kv head) pairs over at most max_len positions:
 // enough CTAs to fill the GPU several times, each split a whole number of tiles.
 
-template <typename T, int GM>
+template <typename T, int GM, bool ROPE>
 int launch_group(const AttnArgs& a, size_t smem, cudaStream_t stream) {
   const dim3 grid(a.splits, a.hkv, static_cast<unsigned>(a.batch));
   auto go = [&](auto kernel) {
@@ -443,43 +505,46 @@ int launch_group(const AttnArgs& a, size_t smem, cudaStream_t stream) {
   const int dpl = (a.hd + 31) / 32;
   if (a.hd % 32 == 0 && (dpl & (dpl - 1)) == 0) {  // head_dim 32, 64, 128, 256: contiguous lanes
     switch (dpl) {
-      case 1: return go(attention_split_kernel<T, GM, 1, true>);
-      case 2: return go(attention_split_kernel<T, GM, 2, true>);
-      case 4: return go(attention_split_kernel<T, GM, 4, true>);
-      default: return go(attention_split_kernel<T, GM, 8, true>);
+      case 1: return go(attention_split_kernel<T, GM, 1, true, ROPE>);
+      case 2: return go(attention_split_kernel<T, GM, 2, true, ROPE>);
+      case 4: return go(attention_split_kernel<T, GM, 4, true, ROPE>);
+      default: return go(attention_split_kernel<T, GM, 8, true, ROPE>);
     }
   }
   // any other head_dim: strided lanes, the smallest power-of-two count covering it
-  if (dpl <= 1) return go(attention_split_kernel<T, GM, 1, false>);
-  if (dpl <= 2) return go(attention_split_kernel<T, GM, 2, false>);
-  if (dpl <= 4) return go(attention_split_kernel<T, GM, 4, false>);
-  return go(attention_split_kernel<T, GM, 8, false>);
+  if (dpl <= 1) return go(attention_split_kernel<T, GM, 1, false, ROPE>);
+  if (dpl <= 2) return go(attention_split_kernel<T, GM, 2, false, ROPE>);
+  if (dpl <= 4) return go(attention_split_kernel<T, GM, 4, false, ROPE>);
+  return go(attention_split_kernel<T, GM, 8, false, ROPE>);
 }
 
-template <typename T>
+template <typename T, bool ROPE = false>
 int launch(AttnArgs a, cudaStream_t stream) {
   const size_t smem = sizeof(float) * (static_cast<size_t>(a.group) * a.hd + a.group * kThreads +
                                        static_cast<size_t>(kWarps) * a.group * a.hd);
   int st;
   if (a.group <= 1) {
-    st = launch_group<T, 1>(a, smem, stream);
+    st = launch_group<T, 1, ROPE>(a, smem, stream);
   } else if (a.group <= 2) {
-    st = launch_group<T, 2>(a, smem, stream);
+    st = launch_group<T, 2, ROPE>(a, smem, stream);
   } else if (a.group <= 4) {
-    st = launch_group<T, 4>(a, smem, stream);
+    st = launch_group<T, 4, ROPE>(a, smem, stream);
   } else if (a.group <= 8) {
-    st = launch_group<T, 8>(a, smem, stream);
+    st = launch_group<T, 8, ROPE>(a, smem, stream);
   } else {
-    st = launch_group<T, 16>(a, smem, stream);
+    st = launch_group<T, 16, ROPE>(a, smem, stream);
   }
   if (st != BM_OK || a.splits == 1) return st;
   return launch_combine<T>(a, stream);
 }
 
 
-// One instance per storage type, each in its own translation unit.
+// One instance per storage type, each in its own translation unit; the _rope
+// forms are the ROPE kernels (the new token rotated and stored in the same launch).
 int launch_f32(const AttnArgs& a, cudaStream_t stream);
 int launch_bf16(const AttnArgs& a, cudaStream_t stream);
+int launch_f32_rope(const AttnArgs& a, cudaStream_t stream);
+int launch_bf16_rope(const AttnArgs& a, cudaStream_t stream);
 
 // The tensor-core kernel (attention_tc.cu): bf16 caches with head_dim 128.
 bool tc_eligible(const AttnArgs& a, bm_dtype_t dtype);

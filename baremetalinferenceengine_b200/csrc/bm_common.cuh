@@ -142,6 +142,17 @@ __device__ __forceinline__ float swiglu1(float g, float u) {
   }
 }
 
+// One RoPE pair, HF half-split (src/kernels.cu:131-139): element i and i + hd/2
+// at angle (cos, sin) become (first cos - second sin, second cos + first sin).
+// The roundings are spelled out (one product rounded, then one fused multiply-add)
+// so the compiler cannot contract the expression differently in different
+// kernels: every kernel that rotates calls this, and a fused form's results equal
+// the RoPE kernels' bit for bit.
+__device__ __forceinline__ void rope_rotate(float first, float second, float2 cs, float* o1, float* o2) {
+  *o1 = __fmaf_rn(first, cs.x, -__fmul_rn(second, cs.y));
+  *o2 = __fmaf_rn(second, cs.x, __fmul_rn(first, cs.y));
+}
+
 // Butterfly sum: every lane of the warp gets the total.
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

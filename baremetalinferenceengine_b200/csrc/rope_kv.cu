@@ -70,9 +70,7 @@ __device__ __forceinline__ void rotate(Chunk<T, VEC>& c1, Chunk<T, VEC>& c2, con
   c2.get(x2);
 #pragma unroll
   for (int e = 0; e < VEC; ++e) {
-    const float first = x1[e], second = x2[e];
-    x1[e] = first * cs[e].x - second * cs[e].y;
-    x2[e] = second * cs[e].x + first * cs[e].y;
+    rope_rotate(x1[e], x2[e], cs[e], &x1[e], &x2[e]);
   }
   c1.set(x1);
   c2.set(x2);

@@ -123,9 +123,7 @@ __device__ __forceinline__ void finish_unit(const RopeArgs& a, const Unit& u, in
 #pragma unroll
   for (int e = 0; e < VEC; ++e) {
     const float2 t = cs[u.c * VEC + e];  // (cos, sin)
-    const float first = x1[e], second = x2[e];
-    x1[e] = first * t.x - second * t.y;
-    x2[e] = second * t.x + first * t.y;
+    rope_rotate(x1[e], x2[e], t, &x1[e], &x2[e]);
   }
   c1.set(x1);
   c2.set(x2);

@@ -192,16 +192,26 @@ void ExecutionEngine::run(int T, int max_len) {
             "bm_rmsnorm_gemm");
       if (delta) std::swap(h, h_next);
     }
-    // Token t at cache position positions_[t] of the one sequence the reference's cache holds.
-    check(bm_rope_kv_store(q_, k_, v_, positions_, 0, nullptr, k_cache, v_cache, rope_table_->get(),
-                           max_seq, config_.rope_theta, T, heads, heads, head_dim, max_seq, 1, BM_F32, nullptr,
-                           stream_),
-          "bm_rope_kv_store");
-    // All T tokens' attention in one launch: query t over cache positions [0, lens_[t]).
-    check(bm_decode_attention(attention_out_, q_, k_cache, v_cache, nullptr, lens_, max_len, T, heads,
-                              heads, head_dim, max_seq, 1, 0.f, attention_workspace_->get(),
-                              attention_workspace_->size(), BM_F32, nullptr, stream_),
-          "bm_decode_attention");
+    if (T == 1) {
+      // A decode step (:113-116): the token's RoPE, its K/V store at positions_[0] and
+      // its attention over [0, lens_[0]) in one launch.
+      check(bm_rope_kv_decode_attention(attention_out_, q_, k_, v_, positions_, rope_table_->get(), max_seq,
+                                        nullptr, k_cache, v_cache, lens_, max_len, 1, heads, heads, head_dim,
+                                        max_seq, 1, 0.f, attention_workspace_->get(), attention_workspace_->size(),
+                                        BM_F32, nullptr, stream_),
+            "bm_rope_kv_decode_attention");
+    } else {
+      // Token t at cache position positions_[t] of the one sequence the reference's cache holds.
+      check(bm_rope_kv_store(q_, k_, v_, positions_, 0, nullptr, k_cache, v_cache, rope_table_->get(),
+                             max_seq, config_.rope_theta, T, heads, heads, head_dim, max_seq, 1, BM_F32, nullptr,
+                             stream_),
+            "bm_rope_kv_store");
+      // All T tokens' attention in one launch: query t over cache positions [0, lens_[t]).
+      check(bm_decode_attention(attention_out_, q_, k_cache, v_cache, nullptr, lens_, max_len, T, heads,
+                                heads, head_dim, max_seq, 1, 0.f, attention_workspace_->get(),
+                                attention_workspace_->size(), BM_F32, nullptr, stream_),
+            "bm_decode_attention");
+    }
     launch_gemm(projected_, attention_out_, w.o_proj, T, dim, dim, stream_);
     // The attention residual add (:118), the FFN norm (:121) and the gate and up
     // projections with the SwiGLU in the epilogue (:122-124): one launch.

@@ -269,6 +269,30 @@ int bm_decode_attention(void* out, const void* q, const void* k_cache, const voi
                         int32_t num_seqs, float scale, void* workspace, size_t workspace_bytes,
                         bm_dtype_t dtype, int32_t* d_status, void* stream);
 
+/* Decode attention with the new token's RoPE and K/V store in the same launch:
+ * the engine's step for one token, launch_rope + launch_kv_store twice +
+ * launch_attention (src/execution_engine.cu:113-116), equivalent to
+ *   bm_rope_kv_store(q, k, v, positions, 0, seq_ids, k_cache, v_cache, rope_table, ...)
+ *   bm_decode_attention(out, q, k_cache, v_cache, seq_ids, lens, ...)
+ * for queries whose token sits at positions[b] < lens[b] of its own sequence (no
+ * two queries of one call share a sequence). k and v are [batch][num_kv_heads]
+ * [head_dim]; rope_table is required (bm_rope_table_*, rope_table_len positions).
+ * On the CUDA-core path (head_dims other than 128) ONE launch: the CTA that attends
+ * to the new position rotates k into the K cache, copies v into the V cache and
+ * every CTA rotates its queries as it stages them, with the arithmetic of
+ * bm_rope_kv_store. Head_dim 128 caches, read by TMA-fed kernels, take the two
+ * calls. q is consumed: afterwards it holds its input or its rotation. On the
+ * one-launch path a position outside [0, lens[b]) or past the table flags
+ * BM_DEVERR_BAD_POSITION and that token is neither rotated nor stored (its query
+ * attends over the cache as it is); the two-call path checks positions as
+ * bm_rope_kv_store does. */
+int bm_rope_kv_decode_attention(void* out, void* q, const void* k, const void* v, const int32_t* positions,
+                                const void* rope_table, int32_t rope_table_len, const int32_t* seq_ids,
+                                void* k_cache, void* v_cache, const int32_t* lens, int32_t max_len, int64_t batch,
+                                int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t max_seq,
+                                int32_t num_seqs, float scale, void* workspace, size_t workspace_bytes,
+                                bm_dtype_t dtype, int32_t* d_status, void* stream);
+
 /* Decode attention that allocates nothing, for callers that cannot call
  * cudaMalloc (a host application whose own arena owns all device memory, a
  * plugin in a process that reserved the GPU up front, a latency-critical path
