@@ -91,6 +91,19 @@ FAKE = 0x100000  # never dereferenced: every call below fails or returns before 
 PTRS3 = (ctypes.c_void_p * 3)(FAKE, FAKE, FAKE)  # host arrays of (fake) device pointers
 WIDTHS3 = (ctypes.c_int32 * 3)(8, 8, 8)
 WIDTHS_BAD = (ctypes.c_int32 * 3)(8, -1, 8)
+WIDTHS_UNEQUAL = (ctypes.c_int32 * 3)(8, 16, 8)
+
+
+def rope_attn(L, table=FAKE, table_len=8, positions=FAKE, hd=64, batch=1):
+    """bm_rope_kv_decode_attention with fake pointers: 2 heads, max_seq 8, fp32."""
+    return L.bm_rope_kv_decode_attention(FAKE, FAKE, FAKE, FAKE, positions, table, table_len, None, FAKE, FAKE,
+                                         FAKE, 8, batch, 2, 2, hd, 8, 1, 0.0, None, 0, 0, None, None)
+
+
+def norm_gemm(L, c=PTRS3, h=FAKE, d=None, res=None, normed=FAKE * 8, widths=WIDTHS3, count=3, swiglu=0, m=4, k=8,
+              dtype=0):
+    """bm_rmsnorm_gemm with fake pointers."""
+    return L.bm_rmsnorm_gemm(c, h, d, FAKE, 1e-5, res, normed, PTRS3, widths, count, swiglu, m, k, dtype, None, None)
 
 
 @pytest.mark.parametrize("call", [
@@ -153,6 +166,20 @@ WIDTHS_BAD = (ctypes.c_int32 * 3)(8, -1, 8)
     lambda L: L.bm_gemm_shared_a(PTRS3, FAKE, PTRS3, WIDTHS3, 4, 4, 8, 0, None, None),     # count 4
     lambda L: L.bm_gemm_shared_a(PTRS3, None, PTRS3, WIDTHS3, 3, 4, 8, 0, None, None),     # NULL a
     lambda L: L.bm_gemm_shared_a(PTRS3, FAKE, PTRS3, WIDTHS3, 3, 4, 8, 9, None, None),     # bad dtype
+    lambda L: norm_gemm(L, c=None),                                                   # NULL output array
+    lambda L: norm_gemm(L, count=0),                                                  # count 0
+    lambda L: norm_gemm(L, swiglu=1),                                                 # swiglu takes 2 weights
+    lambda L: norm_gemm(L, count=2, swiglu=1, widths=WIDTHS_UNEQUAL),                 # gate / up widths differ
+    lambda L: norm_gemm(L, k=0),                                                      # empty rows: no norm
+    lambda L: norm_gemm(L, normed=None),                                              # NULL scratch
+    lambda L: norm_gemm(L, d=FAKE * 4, res=FAKE),                                     # residual_out over h
+    lambda L: norm_gemm(L, d=FAKE * 4, res=FAKE * 4 + 16),                            # residual_out over d
+    lambda L: norm_gemm(L, dtype=9),                                                  # bad dtype
+    lambda L: rope_attn(L, table=None),                                               # the table is required
+    lambda L: rope_attn(L, table_len=0),                                              # empty table
+    lambda L: rope_attn(L, table=FAKE + 4),                                           # table misaligned
+    lambda L: rope_attn(L, positions=None),                                           # NULL positions
+    lambda L: rope_attn(L, hd=6),                                                     # rows not 16-byte vectors
     lambda L: L.bm_selftest_bounded_wait(1000, FAKE, FAKE, None),                     # limit below 1 ms
     lambda L: L.bm_selftest_bounded_wait(10**10, FAKE, FAKE, None),                   # limit above 2 s
     lambda L: L.bm_selftest_bounded_wait(50 * 10**6, None, FAKE, None),               # NULL status
@@ -179,6 +206,8 @@ def test_host_checks_reject_before_any_launch(lib, call):
     lambda L: L.bm_gemm(FAKE, FAKE, FAKE, 0, 5, 7, 0, None, None),
     lambda L: L.bm_softmax(FAKE, 0, 4, 8, 0, None),
     lambda L: L.bm_softmax(FAKE, 8, 0, 8, 0, None),
+    lambda L: norm_gemm(L, m=0),
+    lambda L: rope_attn(L, batch=0),
 ])
 def test_empty_calls_are_no_ops(lib, call):
     assert call(lib) == _lib.BM_OK
