@@ -104,7 +104,7 @@ NVML_REASONS = {
 class ClockSampler:
     """Samples SM clock and clock-event reasons through NVML (read-only) while running."""
 
-    def __init__(self, torch_device, period_s: float = 0.01):
+    def __init__(self, torch_device, period_s: float = 0.002):
         self.samples, self.period, self.err = [], period_s, None
         self._stop = threading.Event()
         self._thread = None
@@ -155,7 +155,7 @@ class ClockSampler:
         reasons = sorted(name for bit, name in NVML_REASONS.items() if mask & bit)
         return {"sm_mhz": statistics.median(s for s, _ in self.samples) if self.samples else None,
                 "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples),
-                "source": "NVML every 10 ms during the timed region"}
+                "source": f"NVML every {self.period * 1e3:g} ms during the timed region"}
 
 
 # ----------------------------------------------------------------------------- CPU side (oracle)
