@@ -241,3 +241,44 @@ def test_workspace_size_and_argument_checks(cuda):
         st = L.bm_decode_attention(p, p, p, p, None, lens.data_ptr(), 1, args[0], args[1], args[2], args[3], 8, 1,
                                    0.0, None, 0, 0, None, None)
         assert st == _lib.BM_ERR_INVALID_ARGUMENT, args
+
+
+@pytest.mark.parametrize("batch,hq,hkv,max_seq,lens", [
+    (1, 32, 8, 8192, [8192]),            # one 8192-position sequence: 8 pairs, 16 splits each
+    (2, 64, 8, 8192, [5000, 8192]),      # two ragged 70B queries
+    (3, 32, 8, 4096, [4096, 700, 1]),    # a query whose splits are mostly empty
+])
+def test_tensor_core_grid_with_a_stale_workspace(cuda, batch, hq, hkv, max_seq, lens):
+    """Below the balanced kernel's minimum, bf16 head_dim 128 runs the per-(query,
+    kv head, split) tensor-core grid, its splits' partials passing through the
+    caller's workspace to the merge kernel. A workspace holding garbage, a zeroed
+    one, and the previous call's leftovers give the same bits, within the tolerance
+    of the oracle: no path reads a slot that the call did not write first."""
+    dt, hd = torch.bfloat16, 128
+    g = gen(batch * 31 + hq)
+    q = randn((batch, hq, hd), dt, g)
+    kc, vc = randn((batch, hkv, max_seq, hd), dt, g), randn((batch, hkv, max_seq, hd), dt, g)
+    seq_ids = torch.arange(batch, dtype=torch.int32)
+    lens_t = torch.tensor(lens, dtype=torch.int32)
+    L = _lib.load()
+    need = ctypes.c_size_t()
+    _lib.check(L.bm_decode_attention_workspace_size(batch, hq, hkv, hd, max_seq, ctypes.byref(need)))
+    ws = torch.empty(need.value, dtype=torch.uint8, device=cuda)
+    qd, kd, vd, sd, ld = q.to(cuda), kc.to(cuda), vc.to(cuda), seq_ids.to(cuda), lens_t.to(cuda)
+    status = ops.DeviceStatus(cuda)
+    outs = []
+    for fill in (0xFF, 0x00, None):  # garbage, zeros, and the previous call's leftovers
+        if fill is not None:
+            ws.fill_(fill)
+        out = torch.full((batch, hq, hd), 7.0, dtype=dt, device=cuda)
+        _lib.check(L.bm_decode_attention(out.data_ptr(), qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), sd.data_ptr(),
+                                         ld.data_ptr(), max_seq, batch, hq, hkv, hd, max_seq, batch, 0.0,
+                                         ws.data_ptr(), need.value, ops.bm_dtype(q), status.ptr,
+                                         torch.cuda.current_stream(cuda).cuda_stream))
+        outs.append(out.cpu())
+    torch.cuda.synchronize(cuda)
+    assert status.read() == 0
+    assert bits_equal(outs[0], outs[1]) and bits_equal(outs[1], outs[2])
+    want, bad = oracle_attention(q, kc, vc, seq_ids, lens_t)
+    assert bad == 0
+    assert orc.worst_error(to_np(outs[2]), want) <= TOL[dt]
