@@ -40,10 +40,17 @@ constexpr int kStagedMinTiles = BM_ATTN_STAGED_MIN_TILES;
 constexpr int kCudaCoreMinTiles = 2;
 
 // min_tiles: the fewest tiles a split may hold (the tensor-core kernel pays a
-// fixed start-up per CTA, so its splits keep at least four tiles).
+// fixed start-up per CTA, so its splits keep at least four tiles). The CUDA-core
+// kernel fits several CTAs on an SM: its plan aims at four CTAs per SM. The staged
+// kernels (tensor-core and TMA-fed, min_tiles kStagedMinTiles) hold one CTA per SM
+// and pay their start-up again in every wave, so with fewer pairs than SMs theirs
+// aims at one wave (at most one CTA per SM); with more, many short CTAs keep the last
+// wave's idle tail small, as on CUDA cores.
 void plan_splits(int64_t pairs, int max_len, int sms, int* splits, int* split_len, int min_tiles = 1) {
   const int tiles = (max_len + kThreads - 1) / kThreads;
-  const int64_t want = std::max<int64_t>(1, (static_cast<int64_t>(sms) * 4 + pairs - 1) / pairs);
+  const int64_t want = min_tiles >= kStagedMinTiles && pairs < sms
+                           ? std::max<int64_t>(1, sms / pairs)
+                           : std::max<int64_t>(1, (static_cast<int64_t>(sms) * 4 + pairs - 1) / pairs);
   const int n = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, tiles / std::max(min_tiles, 1))));
   const int tiles_per_split = (tiles + n - 1) / n;
   *split_len = tiles_per_split * kThreads;
