@@ -68,6 +68,15 @@ struct StepArgs {
   int32_t* status;
 };
 
+// A 16-byte asynchronous copy from global into shared memory (cp.async, cached in
+// L2 only), and the wait for this thread's outstanding copies.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+               "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // Block-wide sum over THREADS threads; every thread gets it. `part` holds one
 // slot per warp.
 template <int THREADS>
@@ -82,21 +91,25 @@ __device__ __forceinline__ float block_sum(float v, float* part) {
 }
 
 template <typename T, int KV, int THREADS>
-__device__ __forceinline__ void row_job(const StepArgs& a, int64_t row, int tid, float (*part)[kMaxWarps]) {
+__device__ __forceinline__ void row_job(const StepArgs& a, int64_t row, int tid, float (*part)[kMaxWarps],
+                                        uint4* w_s) {
   constexpr int N = VecWidth<T>::value;
-  // Narrow rows also hold the attention norm's weights from the start, so no load
-  // waits behind the first reduction (wider rows read them after it, from L2).
-  constexpr bool kEarlyWeights = KV <= 4;
   const int nv = a.dim / N;
   const int64_t off = row * a.dim;
-  uint4 e[KV], p1[KV], p2[KV], wa[kEarlyWeights ? KV : 1];
+  // Both norms' weights go into shared memory asynchronously (w_s: nv vectors of
+  // w_attn, then nv of w_ffn): they land while the id and the embedding row come
+  // from DRAM, and neither norm waits on a load after its reduction.
+  for (int v = tid; v < nv; v += THREADS) {
+    cp_async16(w_s + v, static_cast<const T*>(a.w_attn) + static_cast<int64_t>(v) * N);
+    cp_async16(w_s + nv + v, static_cast<const T*>(a.w_ffn) + static_cast<int64_t>(v) * N);
+  }
+  uint4 e[KV], p1[KV], p2[KV];
 #pragma unroll
   for (int k = 0; k < KV; ++k) {  // the deltas first: they do not wait for the id
     const int v = tid + k * THREADS;
     if (v < nv) {
       p1[k] = ld_stream(static_cast<const T*>(a.attn_out) + off + static_cast<int64_t>(v) * N);
       p2[k] = ld_stream(static_cast<const T*>(a.ffn_out) + off + static_cast<int64_t>(v) * N);
-      if constexpr (kEarlyWeights) wa[k] = ld_keep(static_cast<const T*>(a.w_attn) + static_cast<int64_t>(v) * N);
     }
   }
   const int32_t id = a.ids[row];
@@ -133,6 +146,7 @@ __device__ __forceinline__ void row_job(const StepArgs& a, int64_t row, int tid,
       }
     }
   }
+  cp_async_wait_all();  // this thread's weight copies; block_sum's barrier then publishes everyone's
   const float scale1 = rsqrtf(block_sum<THREADS>(ss, part[0]) / static_cast<float>(a.dim) + a.eps);
   ss = 0.f;
 #pragma unroll
@@ -140,11 +154,7 @@ __device__ __forceinline__ void row_job(const StepArgs& a, int64_t row, int tid,
     const int v = tid + k * THREADS;
     if (v < nv) {
       float w[N], y[N], d[N];
-      if constexpr (kEarlyWeights) {
-        unpack16<T>(wa[k], w);
-      } else {
-        unpack16<T>(ld_keep(static_cast<const T*>(a.w_attn) + static_cast<int64_t>(v) * N), w);
-      }
+      unpack16<T>(w_s[v], w);
 #pragma unroll
       for (int i = 0; i < N; ++i) y[i] = h[k][i] * scale1 * w[i];
       st_plain(static_cast<T*>(a.y_attn) + off + static_cast<int64_t>(v) * N, pack16<T>(y));
@@ -162,7 +172,7 @@ __device__ __forceinline__ void row_job(const StepArgs& a, int64_t row, int tid,
     const int v = tid + k * THREADS;
     if (v < nv) {
       float w[N], y[N];
-      unpack16<T>(ld_keep(static_cast<const T*>(a.w_ffn) + static_cast<int64_t>(v) * N), w);
+      unpack16<T>(w_s[nv + v], w);
 #pragma unroll
       for (int i = 0; i < N; ++i) y[i] = h[k][i] * scale2 * w[i];
       st_plain(static_cast<T*>(a.y_ffn) + off + static_cast<int64_t>(v) * N, pack16<T>(y));
@@ -232,7 +242,8 @@ __global__ void __launch_bounds__(THREADS) layer_step_small_kernel(StepArgs a) {
   }
   grid_dependency_wait();
   if (job < a.rows) {
-    row_job<T, KV, THREADS>(a, job, tid, part);
+    extern __shared__ uint4 w_s[];  // row jobs: the two norm weight vectors
+    row_job<T, KV, THREADS>(a, job, tid, part, w_s);
   } else if (job < a.rows + a.rope_jobs) {
     ropekv::rope_kv_token<T, N, ropekv::kFused>(a.rope, job - a.rows, tid, THREADS, cs);
   } else {
@@ -251,11 +262,18 @@ int launch_small(const StepArgs& a, cudaStream_t stream) {
   const int64_t blocks = a.rows + a.rope_jobs + a.swiglu_jobs;
   const dim3 grid(static_cast<unsigned>(blocks)), block(threads);
   const char* name = "layer_step_small_kernel";
-  if (threads == 256) return launch_kernel(name, layer_step_small_kernel<T, 8, 256>, grid, block, 0, stream, nullptr, a);
-  if (nv <= 128) return launch_kernel(name, layer_step_small_kernel<T, 1, 128>, grid, block, 0, stream, nullptr, a);
-  if (nv <= 256) return launch_kernel(name, layer_step_small_kernel<T, 2, 128>, grid, block, 0, stream, nullptr, a);
-  if (nv <= 512) return launch_kernel(name, layer_step_small_kernel<T, 4, 128>, grid, block, 0, stream, nullptr, a);
-  return launch_kernel(name, layer_step_small_kernel<T, 8, 128>, grid, block, 0, stream, nullptr, a);
+  const int smem = 2 * nv * 16;  // the row jobs' norm weights
+  auto go = [&](auto kernel) {
+    if (smem > 48 * 1024) {
+      if (int st = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem, name)) return st;
+    }
+    return launch_kernel(name, kernel, grid, block, static_cast<size_t>(smem), stream, nullptr, a);
+  };
+  if (threads == 256) return go(layer_step_small_kernel<T, 8, 256>);
+  if (nv <= 128) return go(layer_step_small_kernel<T, 1, 128>);
+  if (nv <= 256) return go(layer_step_small_kernel<T, 2, 128>);
+  if (nv <= 512) return go(layer_step_small_kernel<T, 4, 128>);
+  return go(layer_step_small_kernel<T, 8, 128>);
 }
 
 bool all_aligned16(std::initializer_list<const void*> ptrs) {
